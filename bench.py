@@ -1,0 +1,356 @@
+"""Benchmark of the B200 attention-backward path (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config c4]
+
+One step = one attention-backward call (fused dS kernel + fused dV kernel) over
+this rank's shard of the workload, inputs resident in HBM.  The workload is a
+BASELINE config (default c4: bs=48, seq_q=seq_kv=640, 80/8 heads, d=128,
+p=0.1), partitioned over ranks by (batch, kv-head) unit with no collective in
+the data path (strong scaling: total work fixed).  Between timed steps L2 is
+flushed by writing a 256 MiB buffer (as eval_modal_attn_bwd.py:228-231 does).
+
+value = algorithmic bytes of the whole job / max-over-ranks device time, in
+GB/s; algorithmic bytes = 7·E + |dO| + 2·|V| (P, P_drop, dS at 2 B, mask at
+1 B per score element E = bs·80·sq·skv).
+
+--impl reference times the reference's CPU implementation (the oracle
+restatement of attn_bwd/starting_point.py:27-70) on the host cores, on rank 0.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "sol-1-advisor-token-fix_b200")
+for _p in (ROOT, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "attn-bwd µs per call and achieved HBM GB/s (% of roofline) at 1/2/4/8 B200"
+CONFIGS = {"c0": (2, 64, 96), "c1": (6, 384, 384), "c2": (12, 301, 467),
+           "c3": (2, 2048, 3072), "c4": (48, 640, 640)}
+H, KVH, G, D = 80, 8, 10, 128
+FALLBACK_HBM_GBS = 6650.0
+
+
+def alg_bytes(units, sq, skv):
+    """Algorithmic (minimum unique) HBM bytes for `units` (batch, kv-head) units."""
+    E = units * G * sq * skv
+    dO = units * G * sq * D * 2
+    V = units * skv * D * 2
+    return {"total": 7 * E + dO + 2 * V, "ds": 5 * E + dO + V, "dv": 2 * E + dO + V, "E": E}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def shard_range(n_units, rank, world):
+    return n_units * rank // world, n_units * (rank + 1) // world
+
+
+def make_shard_inputs(bs, sq, skv, u0, u1, seed, device):
+    """Full dO and V, and P / P_drop / mask for heads of units [u0, u1) only."""
+    from attn_bwd_b200.generate import generate_input
+    nh = (u1 - u0) * G
+    dO = torch.empty(bs, sq, H, D, dtype=torch.bfloat16, device=device)
+    V = torch.empty(bs, KVH, skv, D, dtype=torch.bfloat16, device=device)
+    P = torch.empty(nh, sq, skv, dtype=torch.bfloat16, device=device)
+    Pd = torch.empty_like(P)
+    M = torch.empty(nh, sq, skv, dtype=torch.bool, device=device)
+    h_lo, h_hi = u0 * G, u1 * G
+    for b in range(bs):
+        d_b, p_b, pd_b, v_b, m_b, p = generate_input(1, sq, skv, seed * 1000 + b, device=device)
+        dO[b].copy_(d_b[0])
+        V[b].copy_(v_b[0])
+        lo, hi = max(h_lo, b * H), min(h_hi, (b + 1) * H)
+        if lo < hi:
+            P[lo - h_lo:hi - h_lo].copy_(p_b[0, lo - b * H:hi - b * H])
+            Pd[lo - h_lo:hi - h_lo].copy_(pd_b[0, lo - b * H:hi - b * H])
+            M[lo - h_lo:hi - h_lo].copy_(m_b[0, lo - b * H:hi - b * H])
+        del d_b, p_b, pd_b, v_b, m_b
+    return dO, P, Pd, V, M, 0.1
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the background."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = str(gpu_index)
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "100", "-i", self.idx], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        self.windows = []
+
+    def mark(self, t0, t1):
+        self.windows.append((t0, t1))
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.count(",") >= 9]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], [], set()
+        for r in rows:
+            try:
+                ts = time.mktime(time.strptime(r[0].split(".")[0], "%Y/%m/%d %H:%M:%S")) + \
+                    float("0." + r[0].split(".")[1]) if "." in r[0] else 0.0
+            except Exception:
+                ts = None
+            if ts is not None and self.windows and not any(a - 0.15 <= ts <= b + 0.15 for a, b in self.windows):
+                continue
+            try:
+                sm.append(float(r[2]))
+                mx.append(float(r[3]))
+            except ValueError:
+                continue
+            for name, col in (("hw_slowdown", 6), ("hw_thermal_slowdown", 7), ("sw_thermal_slowdown", 8),
+                              ("sw_power_cap", 9)):
+                if r[col].strip() == "Active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def timed_loop(fn, steps, flush, stream):
+    """Per-step CUDA-event times (ms) on the launching stream, L2 flushed between steps."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(i)
+        evs[i][0].record(stream)
+        fn()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.item()
+
+
+def cpu_sample(cfg, units_target_s=12.0, max_units=64):
+    """Times the CPU oracle on whole (batch, kv-head) units of the config until
+    about `units_target_s` seconds have passed.  Returns (GB/s, units, seconds)."""
+    from attn_bwd_b200.generate import generate_input
+    from oracle.attn_bwd_oracle import _attn_bwd_group
+    bs, sq, skv = CONFIGS[cfg]
+    torch.set_num_threads(os.cpu_count() or 1)
+    d = generate_input(1, sq, skv, 4242)
+    sub = (d[0][:, :, :G].contiguous(), d[1][:, :G].contiguous(), d[2][:, :G].contiguous(),
+           d[3][:, :1].contiguous(), d[4][:, :G].contiguous(), d[5])
+    _attn_bwd_group(sub)  # warm-up
+    n, t_total = 0, 0.0
+    while t_total < units_target_s and n < max_units:
+        t0 = time.perf_counter()
+        _attn_bwd_group(sub)
+        t_total += time.perf_counter() - t0
+        n += 1
+    gbs = alg_bytes(n, sq, skv)["total"] / t_total / 1e9
+    return gbs, n, t_total
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    bs, sq, skv = CONFIGS[args.config]
+    from attn_bwd_b200.generate import generate_input
+    from oracle.attn_bwd_oracle import _attn_bwd_group
+    torch.set_num_threads(os.cpu_count() or 1)
+    d = generate_input(1, sq, skv, 4242)
+    sub = (d[0][:, :, :G].contiguous(), d[1][:, :G].contiguous(), d[2][:, :G].contiguous(),
+           d[3][:, :1].contiguous(), d[4][:, :G].contiguous(), d[5])
+    units_per_step = 2
+    for _ in range(args.warmup):
+        for _u in range(units_per_step):
+            _attn_bwd_group(sub)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for _u in range(units_per_step):
+            _attn_bwd_group(sub)
+        times.append(time.perf_counter() - t0)
+    t = sum(times)
+    gbs = alg_bytes(units_per_step * args.steps, sq, skv)["total"] / t / 1e9
+    n_units = bs * KVH
+    us_call = (t / (units_per_step * args.steps)) * n_units * 1e6
+    cores = torch.get_num_threads()
+    sample = f"{units_per_step} of {n_units} (batch, kv-head) units of {args.config} per step"
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t / args.steps * 1e3, 3), "us_per_call": round(us_call, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, eval_modal_attn_bwd.py:139-169 distribution)",
+            "config": {"workload": f"{args.config} bs={bs} seq_q={sq} seq_kv={skv} heads=80/8 d=128 p=0.1",
+                       "sample": sample},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    import attn_bwd_b200 as ab
+
+    bs, sq, skv = CONFIGS[args.config]
+    n_units = bs * KVH
+    u0, u1 = shard_range(n_units, rank, world)
+    dev = torch.device("cuda", local)
+    data = make_shard_inputs(bs, sq, skv, u0, u1, 1000 + int(args.config[1]), dev)
+    dO, P, Pd, V, M, p = data
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        return ab.attn_bwd_shard(data, u0, u1)
+
+    def ds_only():
+        return ab.ds_shard(dO, P, V, M, p, u0, u1)
+
+    def dv_only():
+        return ab.dv_shard(dO, Pd, V, u0, u1)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert ab.poll_error() == 0
+
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    time.sleep(0.3)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    w0 = time.time()
+    step_ms = timed_loop(step, args.steps, flush, stream)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    w1 = time.time()
+    ds_ms = timed_loop(ds_only, args.steps, flush, stream)
+    dv_ms = timed_loop(dv_only, args.steps, flush, stream)
+    w2 = time.time()
+    sampler.mark(w0, w2)
+    time.sleep(0.25)
+    clocks = sampler.stop()
+    assert ab.poll_error() == 0
+
+    t_step = max_over_ranks(sum(step_ms) / 1e3, world)          # seconds for K steps, max over ranks
+    t_ds = max_over_ranks(sum(ds_ms) / args.steps / 1e3, world)  # seconds per launch
+    t_dv = max_over_ranks(sum(dv_ms) / args.steps / 1e3, world)
+    job = alg_bytes(n_units, sq, skv)
+    mine = alg_bytes(u1 - u0, sq, skv)
+    value = job["total"] * args.steps / t_step / 1e9
+    peak, peak_kind = peaks()
+    ds_gbs = mine["ds"] / t_ds / 1e9
+    dv_gbs = mine["dv"] / t_dv / 1e9
+
+    # ---- end to end through the public API with host buffers (pinned), copies timed
+    host = [t.cpu().pin_memory() for t in (dO, P, Pd, V, M)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    dS_h = torch.empty((u1 - u0) * G, sq, skv, dtype=torch.bfloat16).pin_memory()
+    dV_h = torch.empty(u1 - u0, skv, D, dtype=torch.bfloat16).pin_memory()
+    d2h = dS_h.numel() * 2 + dV_h.numel() * 2
+    dev_in = [torch.empty_like(t, device=dev) for t in host]
+
+    def e2e_step():
+        for d_, h_ in zip(dev_in, host):
+            d_.copy_(h_, non_blocking=True)
+        s_, v_ = ab.attn_bwd_shard(tuple(dev_in) + (p,), u0, u1)
+        dS_h.copy_(s_, non_blocking=True)
+        dV_h.copy_(v_, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e2e_ms = timed_loop(e2e_step, args.e2e_steps, flush, stream)
+    t_e2e = max_over_ranks(sum(e2e_ms) / 1e3, world)
+    e2e_val = job["total"] * args.e2e_steps / t_e2e / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, n, secs = cpu_sample(args.config)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{n} (batch, kv-head) units of {args.config} ({n}/{n_units} of the workload), "
+                         f"{secs:.1f} s, oracle restatement of starting_point.py on the host CPU"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_step / args.steps * 1e3, 4),
+            "us_per_call": round(t_step / args.steps * 1e6, 2),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, eval_modal_attn_bwd.py:139-169 distribution)",
+            "config": {"workload": f"{args.config}: bs={bs} seq_q={sq} seq_kv={skv} heads=80/8 d=128 p=0.1",
+                       "partition": f"(batch, kv-head) units, {n_units} over {world} rank(s)",
+                       "l2": "256 MiB buffer written between timed steps; inputs also exceed L2",
+                       "alg_bytes_per_call": job["total"]},
+            "roofline": {"bound": "hbm", "kernel": "ds_kernel", "achieved": round(ds_gbs, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(ds_gbs / peak, 4), "traffic": None,
+                         "peak_kind": peak_kind,
+                         "alg_bytes_per_launch": mine["ds"], "us_per_launch": round(t_ds * 1e6, 2)},
+            "kernels": {
+                "ds_kernel": {"us": round(t_ds * 1e6, 2), "GBps": round(ds_gbs, 1), "frac": round(ds_gbs / peak, 4)},
+                "dv_kernel": {"us": round(t_dv * 1e6, 2), "GBps": round(dv_gbs, 1), "frac": round(dv_gbs / peak, 4)},
+            },
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e / args.e2e_steps * 1e3, 2)},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,88 @@
+/* attn_bwd_b200.h — C ABI of the B200 (sm_100a) GQA attention-backward path.
+ *
+ * Replaces the hot path of the reference's
+ *   custom_kernel((grad_attn_output, attn_weights, attn_weights_dropped,
+ *                  value_states, dropout_mask, attention_dropout))
+ *       -> (grad_attn_scores, grad_value_states)
+ * (attn_bwd/starting_point.py:27-70; called by eval_modal_attn_bwd.py:273,339,381
+ * and append.py:29-33).  Layout is fixed by the reference (starting_point.py:4-17):
+ *
+ *   grad_attn_output      dO   [bs, seq_q, 80, 128]      bf16
+ *   attn_weights          P    [bs, 80, seq_q, seq_kv]   bf16
+ *   attn_weights_dropped  Pd   [bs, 80, seq_q, seq_kv]   bf16
+ *   value_states          V    [bs, 8, seq_kv, 128]      bf16
+ *   dropout_mask          M    [bs, 80, seq_q, seq_kv]   bool (1 byte, 0 or 1)
+ *   grad_attn_scores      dS   [bs, 80, seq_q, seq_kv]   bf16 (output)
+ *   grad_value_states     dV   [bs, 8, seq_kv, 128]      bf16 (output)
+ *
+ * All pointers are device pointers to contiguous tensors, 16-byte aligned.
+ * Every call is asynchronous on `stream` and allocates nothing.  Returns 0 on
+ * success or one of the ATTN_BWD_E* codes (nothing is launched on error).
+ */
+#ifndef ATTN_BWD_B200_H
+#define ATTN_BWD_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* attn_bwd_stream_t; /* == cudaStream_t */
+
+enum {
+  ATTN_BWD_OK = 0,
+  ATTN_BWD_EINVAL = 1,       /* negative size, unit range outside [0, bs*8], null pointer */
+  ATTN_BWD_EALIGN = 2,       /* a pointer is not 16-byte aligned */
+  ATTN_BWD_EUNSUPPORTED = 3, /* shape has no kernel path */
+  ATTN_BWD_ETMAP = 4,        /* TMA descriptor encoding failed */
+  ATTN_BWD_ECUDA = 5,        /* a CUDA runtime call failed (launch, attribute query) */
+  ATTN_BWD_EDEVICE = 6,      /* current device is not compute capability 10.x */
+  ATTN_BWD_EKERNEL = 7       /* a kernel's bounded wait gave up (see attn_bwd_b200_poll_error) */
+};
+
+/* Full call: both outputs.  Replaces starting_point.py:27-70 (custom_kernel).
+ * attention_dropout follows the reference: the mask and 1/(1-p) are applied
+ * only when attention_dropout > 0 (starting_point.py:51-54). */
+int attn_bwd_b200(const void* grad_attn_output, const void* attn_weights, const void* attn_weights_dropped,
+                  const void* value_states, const uint8_t* dropout_mask, float attention_dropout, int bs,
+                  int seq_q, int seq_kv, void* grad_attn_scores, void* grad_value_states,
+                  attn_bwd_stream_t stream);
+
+/* Sharded call over independent units u = b*8 + kv_head in [unit_begin, unit_end).
+ * grad_attn_output and value_states are the FULL tensors; attn_weights,
+ * attn_weights_dropped, dropout_mask, grad_attn_scores point at the first
+ * element of head 10*unit_begin (i.e. [b0, 10*kvh0, 0, 0]) and hold
+ * (unit_end-unit_begin)*10 heads; grad_value_states points at dV[unit_begin]
+ * and holds (unit_end-unit_begin) [seq_kv,128] slabs.  Same math as
+ * attn_bwd_b200 restricted to those units; the reference has no sharding, this
+ * is the per-GPU call of the multi-GPU partition over batch x KV head. */
+int attn_bwd_b200_shard(const void* grad_attn_output, const void* attn_weights, const void* attn_weights_dropped,
+                        const void* value_states, const uint8_t* dropout_mask, float attention_dropout, int bs,
+                        int seq_q, int seq_kv, int unit_begin, int unit_end, void* grad_attn_scores,
+                        void* grad_value_states, attn_bwd_stream_t stream);
+
+/* The two fused kernels alone (same sharding arguments), for timing and tests.
+ * dS: starting_point.py:44-59.  dV: starting_point.py:61-68. */
+int attn_bwd_b200_ds_shard(const void* grad_attn_output, const void* attn_weights, const void* value_states,
+                           const uint8_t* dropout_mask, float attention_dropout, int bs, int seq_q, int seq_kv,
+                           int unit_begin, int unit_end, void* grad_attn_scores, attn_bwd_stream_t stream);
+int attn_bwd_b200_dv_shard(const void* grad_attn_output, const void* attn_weights_dropped, int bs, int seq_q,
+                           int seq_kv, int unit_begin, int unit_end, void* grad_value_states,
+                           attn_bwd_stream_t stream);
+
+/* Synchronises the current device, returns the code a kernel's bounded wait
+ * recorded since the last poll (0 if none) and clears it.  The reference's
+ * evaluator has no counterpart; it reports exceptions (eval_modal_attn_bwd.py:294-302). */
+int attn_bwd_b200_poll_error(void);
+
+/* Human-readable text for an ATTN_BWD_E* code (static storage). */
+const char* attn_bwd_b200_strerror(int code);
+
+/* ABI version of this library (major*100 + minor). */
+int attn_bwd_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATTN_BWD_B200_H */

@@ -1,0 +1,178 @@
+"""B200 (sm_100a) GQA attention backward behind the reference's entry point.
+
+``custom_kernel(data) -> (grad_attn_scores, grad_value_states)`` keeps the
+signature of the reference's ``attn_bwd/starting_point.py:27-70`` (and of
+``attn_bwd/submission.py``), so it drops in wherever the reference harness calls
+it (``eval_modal_attn_bwd.py:273,339,381``; ``append.py:29-33``).  The work runs
+in two hand-written sm_100a kernels reached through the C-ABI of
+``include/attn_bwd_b200.h``; inputs must be CUDA tensors and there is no CPU
+fallback.
+"""
+import torch
+
+from . import _lib
+from ._lib import AttnBwdError
+
+NUM_ATTENTION_HEADS = 80
+NUM_KEY_VALUE_HEADS = 8
+NUM_GROUPS = NUM_ATTENTION_HEADS // NUM_KEY_VALUE_HEADS
+HEAD_DIM = 128
+
+__all__ = ["custom_kernel", "attn_bwd", "attn_bwd_shard", "ds_shard", "dv_shard", "run",
+           "AttnBwdError", "poll_error", "NUM_ATTENTION_HEADS", "NUM_KEY_VALUE_HEADS", "HEAD_DIM"]
+
+
+def _ptr(t):
+    return ctypes_void(t.data_ptr())
+
+
+def ctypes_void(x):
+    import ctypes
+    return ctypes.c_void_p(x)
+
+
+def _stream():
+    return ctypes_void(torch.cuda.current_stream().cuda_stream)
+
+
+def _prep(t, name, dtype, shape, flexible=False):
+    """Checks one input the way the reference's ops would see it and returns a
+    contiguous, 16-byte-aligned view (a copy only if the caller's is not)."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name}: expected a torch.Tensor, got {type(t).__name__}")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name}: tensor must be on a CUDA device (no CPU path), got {t.device}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name}: expected dtype {dtype}, got {t.dtype}")
+    if tuple(t.shape) != tuple(shape):
+        n = 1
+        for x in shape:
+            n *= x
+        if flexible and t.numel() == n and t.is_contiguous():
+            t = t.view(shape)
+        else:
+            raise ValueError(f"{name}: expected shape {tuple(shape)}, got {tuple(t.shape)}")
+    if not t.is_contiguous() or t.data_ptr() % 16:
+        t = t.contiguous() if t.is_contiguous() is False else t.clone()
+    return t
+
+
+def _shapes(grad_attn_output, value_states):
+    if grad_attn_output.dim() != 4 or value_states.dim() != 4:
+        raise ValueError("grad_attn_output and value_states must be 4-D")
+    bs, sq, h, d = grad_attn_output.shape
+    skv = value_states.shape[2]
+    if h != NUM_ATTENTION_HEADS or d != HEAD_DIM:
+        raise ValueError(f"grad_attn_output must be [bs, seq_q, {NUM_ATTENTION_HEADS}, {HEAD_DIM}], "
+                         f"got {tuple(grad_attn_output.shape)}")
+    return bs, sq, skv
+
+
+def _check_inputs(data, u0=None, u1=None):
+    (dO, P, Pd, V, M, p) = data
+    bs, sq, skv = _shapes(dO, V)
+    if u0 is None:
+        u0, u1 = 0, bs * NUM_KEY_VALUE_HEADS
+    if not (0 <= u0 <= u1 <= bs * NUM_KEY_VALUE_HEADS):
+        raise ValueError(f"unit range [{u0},{u1}) outside [0,{bs * NUM_KEY_VALUE_HEADS}]")
+    nh = (u1 - u0) * NUM_GROUPS
+    full = (u0 == 0 and u1 == bs * NUM_KEY_VALUE_HEADS)
+    sshape = (bs, NUM_ATTENTION_HEADS, sq, skv) if full else (nh, sq, skv)
+    dO = _prep(dO, "grad_attn_output", torch.bfloat16, (bs, sq, NUM_ATTENTION_HEADS, HEAD_DIM))
+    V = _prep(V, "value_states", torch.bfloat16, (bs, NUM_KEY_VALUE_HEADS, skv, HEAD_DIM))
+    if P is not None:
+        P = _prep(P, "attn_weights", torch.bfloat16, sshape, flexible=not full)
+    if Pd is not None:
+        Pd = _prep(Pd, "attn_weights_dropped", torch.bfloat16, sshape, flexible=not full)
+    if M is not None:
+        M = _prep(M, "dropout_mask", torch.bool, sshape, flexible=not full)
+    devs = {t.device for t in (dO, P, Pd, V, M) if t is not None}
+    if len(devs) != 1:
+        raise ValueError(f"all tensors must be on one CUDA device, got {devs}")
+    return dO, P, Pd, V, M, float(p), bs, sq, skv, u0, u1
+
+
+def attn_bwd_shard(data, unit_begin, unit_end, out=None):
+    """Attention backward for units u = b*8 + kv_head in [unit_begin, unit_end).
+
+    ``data`` is the reference tuple, except that attn_weights,
+    attn_weights_dropped and dropout_mask hold only the shard's heads
+    ([(unit_end-unit_begin)*10, seq_q, seq_kv]).  Returns (dS_shard [nh, sq, skv],
+    dV_shard [units, skv, 128]).
+    """
+    dO, P, Pd, V, M, p, bs, sq, skv, u0, u1 = _check_inputs(data, unit_begin, unit_end)
+    nh = (u1 - u0) * NUM_GROUPS
+    with torch.cuda.device(dO.device):
+        if out is None:
+            dS = torch.empty((nh, sq, skv), dtype=torch.bfloat16, device=dO.device)
+            dV = torch.empty((u1 - u0, skv, HEAD_DIM), dtype=torch.bfloat16, device=dO.device)
+        else:
+            dS, dV = out
+        _lib.call("attn_bwd_b200_shard", _ptr(dO), _ptr(P), _ptr(Pd), _ptr(V), _ptr(M), p,
+                  bs, sq, skv, u0, u1, _ptr(dS), _ptr(dV), _stream())
+    return dS, dV
+
+
+def attn_bwd(data, out=None):
+    """Full call; returns fresh (dS [bs,80,sq,skv], dV [bs,8,skv,128]) bf16 tensors
+    unless ``out`` supplies preallocated ones."""
+    dO, P, Pd, V, M, p, bs, sq, skv, u0, u1 = _check_inputs(data)
+    with torch.cuda.device(dO.device):
+        if out is None:
+            dS = torch.empty((bs, NUM_ATTENTION_HEADS, sq, skv), dtype=torch.bfloat16, device=dO.device)
+            dV = torch.empty((bs, NUM_KEY_VALUE_HEADS, skv, HEAD_DIM), dtype=torch.bfloat16, device=dO.device)
+        else:
+            dS, dV = out
+        _lib.call("attn_bwd_b200", _ptr(dO), _ptr(P), _ptr(Pd), _ptr(V), _ptr(M), p,
+                  bs, sq, skv, _ptr(dS), _ptr(dV), _stream())
+    return dS, dV
+
+
+def custom_kernel(data):
+    """Drop-in for the reference's ``custom_kernel`` (starting_point.py:27-70).
+
+    data = (grad_attn_output [bs,sq,80,128] bf16, attn_weights [bs,80,sq,skv] bf16,
+            attn_weights_dropped [bs,80,sq,skv] bf16, value_states [bs,8,skv,128] bf16,
+            dropout_mask [bs,80,sq,skv] bool, attention_dropout float)
+    returns (grad_attn_scores [bs,80,sq,skv] bf16, grad_value_states [bs,8,skv,128] bf16),
+    ordered on ``torch.cuda.current_stream()``.
+    """
+    if not isinstance(data, (tuple, list)) or len(data) != 6:
+        raise ValueError("custom_kernel expects the 6-tuple (grad_attn_output, attn_weights, "
+                         "attn_weights_dropped, value_states, dropout_mask, attention_dropout)")
+    return attn_bwd(tuple(data))
+
+
+@torch.no_grad()
+def run(grad_attn_output, attn_weights, attn_weights_dropped, value_states, dropout_mask,
+        attention_dropout):
+    """Keyword wrapper with the signature of the reference harness's ``run``
+    (append.py:29-33)."""
+    return custom_kernel((grad_attn_output, attn_weights, attn_weights_dropped, value_states,
+                          dropout_mask, attention_dropout))
+
+
+def ds_shard(dO, P, V, M, p, unit_begin, unit_end, out=None):
+    """dS kernel alone (same shard conventions as :func:`attn_bwd_shard`)."""
+    dO, P, _, V, M, p, bs, sq, skv, u0, u1 = _check_inputs((dO, P, None, V, M, p), unit_begin, unit_end)
+    nh = (u1 - u0) * NUM_GROUPS
+    with torch.cuda.device(dO.device):
+        dS = out if out is not None else torch.empty((nh, sq, skv), dtype=torch.bfloat16, device=dO.device)
+        _lib.call("attn_bwd_b200_ds_shard", _ptr(dO), _ptr(P), _ptr(V), _ptr(M), p, bs, sq, skv,
+                  u0, u1, _ptr(dS), _stream())
+    return dS
+
+
+def dv_shard(dO, Pd, V, unit_begin, unit_end, out=None):
+    """dV kernel alone (same shard conventions as :func:`attn_bwd_shard`)."""
+    dO, _, Pd, V, _, _, bs, sq, skv, u0, u1 = _check_inputs((dO, None, Pd, V, None, 0.0), unit_begin, unit_end)
+    with torch.cuda.device(dO.device):
+        dV = out if out is not None else torch.empty((u1 - u0, skv, HEAD_DIM), dtype=torch.bfloat16,
+                                                     device=dO.device)
+        _lib.call("attn_bwd_b200_dv_shard", _ptr(dO), _ptr(Pd), bs, sq, skv, u0, u1, _ptr(dV), _stream())
+    return dV
+
+
+def poll_error():
+    """Synchronise and return (and clear) the code of a kernel wait that gave up; 0 if none."""
+    return _lib.load().attn_bwd_b200_poll_error()

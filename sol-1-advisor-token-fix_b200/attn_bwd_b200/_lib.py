@@ -1,0 +1,63 @@
+"""ctypes binding of the C-ABI in include/attn_bwd_b200.h.
+
+The shared library is built in-tree (``__graft_entry__.build()``) next to this
+file.  There is no fallback: if the library is missing, every entry point
+raises.
+"""
+import ctypes
+import os
+
+LIB_NAME = "libattn_bwd_b200.so"
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+
+# C-ABI error codes (enum in include/attn_bwd_b200.h)
+OK, EINVAL, EALIGN, EUNSUPPORTED, ETMAP, ECUDA, EDEVICE, EKERNEL = range(8)
+
+# Every symbol the header declares, with its ctypes signature.
+_VP, _I, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+SIGNATURES = {
+    "attn_bwd_b200": (_I, [_VP, _VP, _VP, _VP, _VP, _F, _I, _I, _I, _VP, _VP, _VP]),
+    "attn_bwd_b200_shard": (_I, [_VP, _VP, _VP, _VP, _VP, _F, _I, _I, _I, _I, _I, _VP, _VP, _VP]),
+    "attn_bwd_b200_ds_shard": (_I, [_VP, _VP, _VP, _VP, _F, _I, _I, _I, _I, _I, _VP, _VP]),
+    "attn_bwd_b200_dv_shard": (_I, [_VP, _VP, _I, _I, _I, _I, _I, _VP, _VP]),
+    "attn_bwd_b200_poll_error": (_I, []),
+    "attn_bwd_b200_strerror": (ctypes.c_char_p, [_I]),
+    "attn_bwd_b200_version": (_I, []),
+}
+
+_lib = None
+
+
+class AttnBwdError(RuntimeError):
+    """A C-ABI call returned a non-zero ATTN_BWD_E* code."""
+
+    def __init__(self, fn, code):
+        self.code = code
+        super().__init__(f"{fn} failed: {code} ({strerror(code)})")
+
+
+def load():
+    """Load the in-tree library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"attn_bwd_b200 CUDA library not built: {LIB_PATH} is missing "
+                "(run __graft_entry__.build()); there is no CPU fallback")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(lib, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def strerror(code):
+    return load().attn_bwd_b200_strerror(int(code)).decode()
+
+
+def call(name, *args):
+    rc = getattr(load(), name)(*args)
+    if rc != OK:
+        raise AttnBwdError(name, rc)

@@ -1,0 +1,284 @@
+// attn_bwd_b200.cu — C-ABI entry points: argument checks, TMA descriptors,
+// launches of the fused dS and dV kernels on the caller's stream.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/attn_bwd_b200.h"
+#include "ds_kernel.cuh"
+#include "dv_kernel.cuh"
+
+using namespace attn_bwd;
+
+namespace {
+
+__device__ int g_kernel_error = 0;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+  bool ready = false;
+  int rc = ATTN_BWD_OK;
+  int sm_count = 0;
+  int* err = nullptr;  // device address of g_kernel_error on this device
+};
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+EncodeTiledFn g_encode = nullptr;
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ATTN_BWD_ECUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.ready) {
+    st.ready = true;
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+      st.rc = ATTN_BWD_ECUDA;
+    } else if (major != 10) {
+      st.rc = ATTN_BWD_EDEVICE;
+    } else if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+               cudaFuncSetAttribute(ds::ds_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ds::Cfg<false>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(ds::ds_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ds::Cfg<true>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(dv::dv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    dv::Cfg<false>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(dv::dv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    dv::Cfg<true>::SMEM_BYTES) != cudaSuccess ||
+               cudaGetSymbolAddress(reinterpret_cast<void**>(&st.err), g_kernel_error) != cudaSuccess) {
+      st.rc = ATTN_BWD_ECUDA;
+    }
+    if (st.rc == ATTN_BWD_OK && !g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || !fn) {
+        st.rc = ATTN_BWD_ETMAP;
+      } else {
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+      }
+    }
+  }
+  *out = &st;
+  return st.rc;
+}
+
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+              const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(m, dt, rank, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct Shape {
+  int bs, sq, skv, u0, u1;
+  int n_units() const { return u1 - u0; }
+};
+
+int check_shape(const Shape& s) {
+  if (s.bs < 0 || s.sq < 0 || s.skv < 0) return ATTN_BWD_EINVAL;
+  if (s.u0 < 0 || s.u1 < s.u0 || s.u1 > s.bs * kKvHeads) return ATTN_BWD_EINVAL;
+  // TMA descriptor limits: every extent < 2^31 and strides < 2^40 bytes
+  const long long rows = (long long)s.bs * kHeads * s.sq;
+  if ((long long)s.sq * s.skv * 2 >= (1ll << 39) || rows * s.skv >= (1ll << 40) || s.sq >= (1 << 30) ||
+      s.skv >= (1 << 30))
+    return ATTN_BWD_EINVAL;
+  return ATTN_BWD_OK;
+}
+
+// seq_kv rows of P / mask / dS must be 16-byte multiples for the TMA path.
+inline bool tma_rows_ok(int skv) { return (skv % 16) == 0; }
+
+int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void* P, const void* V,
+              const uint8_t* M, float p, void* dS, cudaStream_t stream) {
+  const int nbh = s.n_units() * kGroups;
+  if (nbh == 0 || s.sq == 0 || s.skv == 0) return ATTN_BWD_OK;
+  const bool rag = !tma_rows_ok(s.skv);
+  CUtensorMap tm_dO, tm_V, tm_P, tm_M, tm_dS;
+  std::memset(&tm_P, 0, sizeof(tm_P));
+  std::memset(&tm_M, 0, sizeof(tm_M));
+  std::memset(&tm_dS, 0, sizeof(tm_dS));
+  {
+    cuuint64_t dims[4] = {kHeadDim, kHeads, (cuuint64_t)s.sq, (cuuint64_t)s.bs};
+    cuuint64_t str[3] = {kHeadDim * 2, (cuuint64_t)kHeads * kHeadDim * 2, (cuuint64_t)s.sq * kHeads * kHeadDim * 2};
+    cuuint32_t box[4] = {64, 1, ds::BM, 1};
+    if (!make_map(&tm_dO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dO, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return ATTN_BWD_ETMAP;
+  }
+  {
+    cuuint64_t dims[3] = {kHeadDim, (cuuint64_t)s.skv, (cuuint64_t)s.bs * kKvHeads};
+    cuuint64_t str[2] = {kHeadDim * 2, (cuuint64_t)s.skv * kHeadDim * 2};
+    cuuint32_t box[3] = {64, ds::BN, 1};
+    if (!make_map(&tm_V, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, V, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return ATTN_BWD_ETMAP;
+  }
+  if (!rag) {
+    cuuint64_t dims[3] = {(cuuint64_t)s.skv, (cuuint64_t)s.sq, (cuuint64_t)nbh};
+    cuuint64_t str2[2] = {(cuuint64_t)s.skv * 2, (cuuint64_t)s.sq * s.skv * 2};
+    cuuint64_t str1[2] = {(cuuint64_t)s.skv, (cuuint64_t)s.sq * s.skv};
+    cuuint32_t box[3] = {ds::BN, ds::BM, 1};
+    if (!make_map(&tm_P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, P, dims, str2, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_dS, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dS, dims, str2, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_M, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, M, dims, str1, box, CU_TENSOR_MAP_SWIZZLE_64B))
+      return ATTN_BWD_ETMAP;
+  }
+  ds::Params prm;
+  prm.sq = s.sq;
+  prm.skv = s.skv;
+  prm.n_mb = (s.sq + ds::BM - 1) / ds::BM;
+  prm.n_units = nbh * prm.n_mb;
+  prm.nchunks = (s.skv + ds::BN - 1) / ds::BN;
+  prm.resident = prm.nchunks <= ds::kResidentMaxChunks ? 1 : 0;
+  prm.bh_base = s.u0 * kGroups;
+  prm.use_mask = p > 0.f ? 1 : 0;
+  prm.scale = p > 0.f ? 1.0f / (1.0f - p) : 1.0f;
+  prm.err = st.err;
+  prm.P = static_cast<const uint8_t*>(P);
+  prm.M = M;
+  prm.dS = static_cast<uint8_t*>(dS);
+  const unsigned long long E = (unsigned long long)nbh * s.sq * s.skv;
+  prm.p_end16 = (E * 2 + 15) & ~15ull;
+  prm.m_end16 = (E + 15) & ~15ull;
+  const int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
+  if (rag)
+    ds::ds_kernel<true><<<grid, ds::kThreads, ds::Cfg<true>::SMEM_BYTES, stream>>>(tm_dO, tm_V, tm_P, tm_M, tm_dS, prm);
+  else
+    ds::ds_kernel<false><<<grid, ds::kThreads, ds::Cfg<false>::SMEM_BYTES, stream>>>(tm_dO, tm_V, tm_P, tm_M, tm_dS, prm);
+  return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
+}
+
+int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void* Pd, void* dV,
+              cudaStream_t stream) {
+  const int nu = s.n_units();
+  if (nu == 0 || s.skv == 0) return ATTN_BWD_OK;
+  if (s.sq == 0) {  // empty sum over seq_q: dV = 0
+    const size_t bytes = (size_t)nu * s.skv * kHeadDim * 2;
+    return cudaMemsetAsync(dV, 0, bytes, stream) == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
+  }
+  // P_drop rows need only be 16-byte multiples (seq_kv % 8) for the TMA path
+  const bool rag = (s.skv % 8) != 0;
+  CUtensorMap tm_Pd, tm_dO;
+  std::memset(&tm_Pd, 0, sizeof(tm_Pd));
+  if (!rag) {
+    cuuint64_t dims[3] = {(cuuint64_t)s.skv, (cuuint64_t)s.sq, (cuuint64_t)nu * kGroups};
+    cuuint64_t str[2] = {(cuuint64_t)s.skv * 2, (cuuint64_t)s.sq * s.skv * 2};
+    cuuint32_t box[3] = {64, dv::BK, 1};
+    if (!make_map(&tm_Pd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, Pd, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return ATTN_BWD_ETMAP;
+  }
+  {
+    cuuint64_t dims[4] = {kHeadDim, kHeads, (cuuint64_t)s.sq, (cuuint64_t)s.bs};
+    cuuint64_t str[3] = {kHeadDim * 2, (cuuint64_t)kHeads * kHeadDim * 2, (cuuint64_t)s.sq * kHeads * kHeadDim * 2};
+    cuuint32_t box[4] = {64, 1, dv::BK, 1};
+    if (!make_map(&tm_dO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dO, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return ATTN_BWD_ETMAP;
+  }
+  dv::Params prm;
+  prm.sq = s.sq;
+  prm.skv = s.skv;
+  prm.n_jt = (s.skv + dv::BM - 1) / dv::BM;
+  prm.n_units = nu * prm.n_jt;
+  prm.n_kc = (s.sq + dv::BK - 1) / dv::BK;
+  prm.unit_base = s.u0;
+  prm.err = st.err;
+  prm.Pd = static_cast<const uint8_t*>(Pd);
+  prm.pd_end16 = ((unsigned long long)nu * kGroups * s.sq * s.skv * 2 + 15) & ~15ull;
+  const int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(dV);
+  if (rag)
+    dv::dv_kernel<true><<<grid, dv::Cfg<true>::kThreads, dv::Cfg<true>::SMEM_BYTES, stream>>>(tm_Pd, tm_dO, out, prm);
+  else
+    dv::dv_kernel<false><<<grid, dv::Cfg<false>::kThreads, dv::Cfg<false>::SMEM_BYTES, stream>>>(tm_Pd, tm_dO, out, prm);
+  return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
+}
+
+int prologue(DeviceState** st, const Shape& s) {
+  int rc = check_shape(s);
+  if (rc) return rc;
+  return device_state(st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int attn_bwd_b200_ds_shard(const void* dO, const void* P, const void* V, const uint8_t* M, float p, int bs, int sq,
+                           int skv, int u0, int u1, void* dS, attn_bwd_stream_t stream) {
+  Shape s{bs, sq, skv, u0, u1};
+  DeviceState* st = nullptr;
+  int rc = prologue(&st, s);
+  if (rc) return rc;
+  if (!dO || !P || !V || !M || !dS) return s.n_units() == 0 ? ATTN_BWD_OK : ATTN_BWD_EINVAL;
+  if (!aligned16(dO) || !aligned16(P) || !aligned16(V) || !aligned16(M) || !aligned16(dS)) return ATTN_BWD_EALIGN;
+  return launch_ds(*st, s, dO, P, V, M, p, dS, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int attn_bwd_b200_dv_shard(const void* dO, const void* Pd, int bs, int sq, int skv, int u0, int u1, void* dV,
+                           attn_bwd_stream_t stream) {
+  Shape s{bs, sq, skv, u0, u1};
+  DeviceState* st = nullptr;
+  int rc = prologue(&st, s);
+  if (rc) return rc;
+  if (!dO || !Pd || !dV) return s.n_units() == 0 ? ATTN_BWD_OK : ATTN_BWD_EINVAL;
+  if (!aligned16(dO) || !aligned16(Pd) || !aligned16(dV)) return ATTN_BWD_EALIGN;
+  return launch_dv(*st, s, dO, Pd, dV, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const void* V, const uint8_t* M, float p,
+                        int bs, int sq, int skv, int u0, int u1, void* dS, void* dV, attn_bwd_stream_t stream) {
+  Shape s{bs, sq, skv, u0, u1};
+  DeviceState* st = nullptr;
+  int rc = prologue(&st, s);
+  if (rc) return rc;
+  if (!dO || !P || !Pd || !V || !M || !dS || !dV) return s.n_units() == 0 ? ATTN_BWD_OK : ATTN_BWD_EINVAL;
+  if (!aligned16(dO) || !aligned16(P) || !aligned16(Pd) || !aligned16(V) || !aligned16(M) || !aligned16(dS) ||
+      !aligned16(dV))
+    return ATTN_BWD_EALIGN;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  rc = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
+  if (rc) return rc;
+  return launch_dv(*st, s, dO, Pd, dV, cs);
+}
+
+int attn_bwd_b200(const void* dO, const void* P, const void* Pd, const void* V, const uint8_t* M, float p, int bs,
+                  int sq, int skv, void* dS, void* dV, attn_bwd_stream_t stream) {
+  return attn_bwd_b200_shard(dO, P, Pd, V, M, p, bs, sq, skv, 0, bs * kKvHeads, dS, dV, stream);
+}
+
+int attn_bwd_b200_poll_error(void) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) return ATTN_BWD_ECUDA;
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kernel_error, sizeof(int)) != cudaSuccess) return ATTN_BWD_ECUDA;
+  if (v && cudaMemcpyToSymbol(g_kernel_error, &zero, sizeof(int)) != cudaSuccess) return ATTN_BWD_ECUDA;
+  return v;
+}
+
+const char* attn_bwd_b200_strerror(int code) {
+  switch (code) {
+    case ATTN_BWD_OK: return "ok";
+    case ATTN_BWD_EINVAL: return "invalid argument (size, unit range or null pointer)";
+    case ATTN_BWD_EALIGN: return "tensor pointer is not 16-byte aligned";
+    case ATTN_BWD_EUNSUPPORTED: return "shape has no kernel path";
+    case ATTN_BWD_ETMAP: return "TMA descriptor encoding failed";
+    case ATTN_BWD_ECUDA: return "CUDA runtime call failed";
+    case ATTN_BWD_EDEVICE: return "current device is not a compute capability 10.x (B200) GPU";
+    case ATTN_BWD_EKERNEL: return "a kernel wait timed out";
+    default: return "unknown error";
+  }
+}
+
+int attn_bwd_b200_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,506 @@
+// ds_kernel.cuh — fused dS kernel: dP~ = dO·Vᵀ on tcgen05 (TMEM accumulator),
+// dropout backward and softmax backward in the epilogue, bf16 dS written once.
+//
+// Reference math (attn_bwd/starting_point.py:44-59, same as
+// eval_modal_attn_bwd.py:108-124):
+//   dP~ = dO_h · V_{h/10}ᵀ            (fp32)
+//   dP  = dP~ · mask / (1 - p)        (only when p > 0)
+//   r   = Σ_j dP_ij · P_ij
+//   dS  = bf16(P · (dP − r))
+//
+// Work unit: one (batch·head, 128-row block of seq_q).  A unit is processed in
+// 64-column chunks of seq_kv, twice: pass 1 accumulates the row sums r
+// (thread-per-row, no shuffles), pass 2 forms dS.  The MMA for a chunk is
+// re-issued in pass 2 (dP~ is never written to HBM) unless the whole row
+// fits the TMEM ring with room for the next unit ("resident" mode, seq_kv <=
+// 256), in which case pass 2 re-reads pass 1's TMEM columns.  P and the mask
+// are streamed by TMA in both passes; pass 2 re-reads them from L2.
+//
+// Roles (384 threads):
+//   warp 0  TMA producer for dO tiles and V chunks
+//   warp 1  tcgen05 MMA issuer (also owns the TMEM allocation)
+//   warp 2  TMA producer for P / mask chunks
+//   warp 3  idle
+//   warps 4..11  epilogue; warp w reads TMEM lanes 32·(w%4).. and chunk
+//                columns 32·((w-4)/4) ..+32
+//
+// Two row formats (template flag RAG):
+//   RAG = false  seq_kv % 16 == 0: P / mask chunks are TMA tensor tiles
+//                (128B / 64B swizzle) and dS leaves by TMA tensor store.
+//   RAG = true   any seq_kv: rows of P / mask are not 16-byte aligned, so each
+//                row segment is fetched by its own untiled bulk copy from the
+//                16-byte boundary below it into a padded row (pitch 144 B / 80 B);
+//                the epilogue re-aligns it in registers (funnel shifts), masks
+//                columns >= seq_kv, and stores dS through a per-warp transpose
+//                buffer with coalesced 2-byte stores.
+#pragma once
+#include "sm100.cuh"
+
+namespace attn_bwd {
+
+constexpr int kHeads = 80, kKvHeads = 8, kGroups = 10, kHeadDim = 128;
+
+namespace ds {
+constexpr int BM = 128;          // rows (seq_q) per unit
+constexpr int BN = 64;           // columns (seq_kv) per chunk
+constexpr int TSLOTS = 8;        // TMEM ring: 8 x 64 fp32 columns = 512
+constexpr int VST = 3;           // V chunk stages
+constexpr int kThreads = 384;
+constexpr int kResidentMaxChunks = 4;
+constexpr int DO_BYTES = BM * kHeadDim * 2;   // 32 KB (two 64-column SW128 halves)
+constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
+
+template <bool RAG>
+struct Cfg {
+  static constexpr int PST = RAG ? 3 : 4;              // P/mask chunk stages
+  static constexpr int P_PITCH = RAG ? 144 : 128;      // bytes per staged P row
+  static constexpr int M_PITCH = RAG ? 80 : 64;        // bytes per staged mask row
+  static constexpr int P_BYTES = BM * P_PITCH;
+  static constexpr int M_BYTES = BM * M_PITCH;
+  static constexpr int STG_PITCH = 80;                 // per-warp dS transpose rows (RAG)
+  static constexpr int STG_BYTES = RAG ? 8 * 32 * STG_PITCH : 0;
+  static constexpr int OFF_DO = 0;
+  static constexpr int OFF_V = OFF_DO + 2 * DO_BYTES;
+  static constexpr int OFF_P = OFF_V + VST * V_BYTES;
+  static constexpr int OFF_M = OFF_P + PST * P_BYTES;
+  static constexpr int OFF_STG = OFF_M + PST * M_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
+  // barriers: dO full/empty (2+2), V full/empty, PM full/empty, dS ready, T full/empty, pair (4)
+  static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4;
+  static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][2][128]
+  static constexpr int OFF_MISC = OFF_RX + 2 * 2 * BM * 4;
+  static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024, "dS kernel shared memory");
+};
+
+struct Params {
+  int sq, skv;
+  int n_units;      // local (batch·head) count × row blocks
+  int n_mb;         // row blocks per head
+  int nchunks;      // ceil(skv / 64)
+  int resident;     // 1: pass 2 re-reads pass-1 TMEM columns
+  int bh_base;      // global (batch·head) index of local head 0
+  int use_mask;     // p > 0
+  float scale;      // 1/(1-p) when use_mask, else 1
+  int* err;
+  // raw pointers for the RAG path (local shard bases, 16-byte aligned)
+  const uint8_t* P;
+  const uint8_t* M;
+  uint8_t* dS;
+  unsigned long long p_end16;   // bytes of P rounded up to 16 (bulk copies never read past it)
+  unsigned long long m_end16;   // same for the mask
+};
+
+// Shifts a little-endian byte stream right by `sh` bytes (0..15):
+// out[j] = bytes [4j+sh, 4j+sh+4) of `in`.  `in` holds NOUT+4 words.
+template <int NOUT>
+__device__ __forceinline__ void byte_shift(const uint32_t* in, uint32_t sh, uint32_t* out) {
+  uint32_t u[NOUT + 2], v[NOUT + 1];
+#pragma unroll
+  for (int j = 0; j < NOUT + 2; ++j) u[j] = (sh & 8) ? in[j + 2] : in[j];
+#pragma unroll
+  for (int j = 0; j < NOUT + 1; ++j) v[j] = (sh & 4) ? u[j + 1] : u[j];
+  const uint32_t bits = (sh & 3) * 8;
+#pragma unroll
+  for (int j = 0; j < NOUT; ++j) out[j] = __funnelshift_r(v[j], v[j + 1], bits);
+}
+
+// Loads this thread's 32 P values (16 words of bf16 pairs) and 32 mask bytes
+// (8 words) of one chunk row from the staged chunk.
+template <bool RAG>
+__device__ __forceinline__ void load_row(uint32_t p_stage, uint32_t m_stage, int row, int half, uint32_t shP,
+                                         uint32_t shM, uint32_t (&pw)[16], uint32_t (&mw)[8]) {
+  using namespace sm100;
+  if constexpr (!RAG) {
+    const uint32_t p_row = p_stage + row * 128;
+    const uint32_t m_row = m_stage + row * 64;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 t = lds128(p_row + (((half * 4 + i) ^ (row & 7)) << 4));
+      pw[4 * i] = t.x; pw[4 * i + 1] = t.y; pw[4 * i + 2] = t.z; pw[4 * i + 3] = t.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 t = lds128(m_row + (((half * 2 + i) ^ ((row >> 1) & 3)) << 4));
+      mw[4 * i] = t.x; mw[4 * i + 1] = t.y; mw[4 * i + 2] = t.z; mw[4 * i + 3] = t.w;
+    }
+  } else {
+    uint32_t in[20];
+    const uint32_t p_row = p_stage + row * Cfg<true>::P_PITCH + half * 64;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+      const uint4 t = lds128(p_row + i * 16);
+      in[4 * i] = t.x; in[4 * i + 1] = t.y; in[4 * i + 2] = t.z; in[4 * i + 3] = t.w;
+    }
+    byte_shift<16>(in, shP, pw);
+    const uint32_t m_row = m_stage + row * Cfg<true>::M_PITCH + half * 32;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const uint4 t = lds128(m_row + i * 16);
+      in[4 * i] = t.x; in[4 * i + 1] = t.y; in[4 * i + 2] = t.z; in[4 * i + 3] = t.w;
+    }
+    byte_shift<8>(in, shM, mw);
+  }
+}
+
+// Element e (0..31) of the row: P value, and whether the score is kept.
+__device__ __forceinline__ float p_at(const uint32_t (&pw)[16], int e) {
+  return (e & 1) ? sm100::bf16hi(pw[e >> 1]) : sm100::bf16lo(pw[e >> 1]);
+}
+__device__ __forceinline__ bool m_at(const uint32_t (&mw)[8], int e) {
+  return ((mw[e >> 2] >> ((e & 3) * 8)) & 0xFFu) != 0;
+}
+
+template <bool RAG>
+__global__ void __launch_bounds__(kThreads, 1)
+ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64,1,128,1) SW128
+          const __grid_constant__ CUtensorMap tm_V,    // (d, skv, b·8)  box (64,64,1)    SW128
+          const __grid_constant__ CUtensorMap tm_P,    // (skv, sq, bh)  box (64,128,1)   SW128 (aligned rows only)
+          const __grid_constant__ CUtensorMap tm_M,    // (skv, sq, bh)  box (64,128,1)   SW64 u8 (aligned only)
+          const __grid_constant__ CUtensorMap tm_dS,   // (skv, sq, bh)  box (64,128,1)   SW128 (aligned only)
+          const Params prm) {
+  using namespace sm100;
+  using C = Cfg<RAG>;
+  constexpr int PST = C::PST;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* dO_full = bars + 0;
+  uint64_t* dO_empty = bars + 2;
+  uint64_t* V_full = bars + 4;
+  uint64_t* V_empty = V_full + VST;
+  uint64_t* PM_full = V_empty + VST;
+  uint64_t* PM_empty = PM_full + PST;
+  uint64_t* dS_ready = PM_empty + PST;
+  uint64_t* T_full = dS_ready + PST;
+  uint64_t* T_empty = T_full + TSLOTS;
+  uint64_t* pair_bar = T_empty + TSLOTS;
+  float* rx = reinterpret_cast<float*>(smem + C::OFF_RX);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) { mbar_init(&dO_full[i], 1); mbar_init(&dO_empty[i], 1); }
+    for (int i = 0; i < VST; ++i) { mbar_init(&V_full[i], 1); mbar_init(&V_empty[i], 1); }
+    for (int i = 0; i < PST; ++i) {
+      mbar_init(&PM_full[i], 1);
+      mbar_init(&PM_empty[i], 8);
+      mbar_init(&dS_ready[i], 8);
+    }
+    for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], 8); }
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_dO); prefetch_tmap(&tm_V);
+    if (!RAG) { prefetch_tmap(&tm_P); prefetch_tmap(&tm_M); prefetch_tmap(&tm_dS); }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, TSLOTS * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  const int n_units = prm.n_units, n_mb = prm.n_mb, nchunks = prm.nchunks;
+  const int sq = prm.sq, skv = prm.skv;
+  const bool resident = prm.resident != 0;
+  const int npass_mma = resident ? 1 : 2;
+  int* err = prm.err;
+
+  if (warp == 0) {
+    // ------------------------------------------------ dO / V producer
+    if (lane == 0) {
+      uint32_t vi = 0, di = 0;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const int bhl = u / n_mb, mb = u - bhl * n_mb;
+        const int bh = prm.bh_base + bhl;
+        const int b = bh / kHeads, h = bh - b * kHeads;
+        const int zv = b * kKvHeads + h / kGroups;
+        const int db = di & 1;
+        if (!mbar_wait(&dO_empty[db], ((di >> 1) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
+        mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
+        tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
+        tma_load_4d(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
+        ++di;
+        for (int pass = 0; pass < npass_mma; ++pass) {
+          for (int c = 0; c < nchunks; ++c) {
+            const int vs = vi % VST;
+            if (!mbar_wait(&V_empty[vs], ((vi / VST) & 1) ^ 1, abort_flag, err, 0x0102)) goto producer_done;
+            mbar_arrive_expect_tx(&V_full[vs], V_BYTES);
+            uint8_t* dst = smem + C::OFF_V + vs * V_BYTES;
+            tma_load_3d(dst, &tm_V, &V_full[vs], 0, c * BN, zv);
+            tma_load_3d(dst + V_BYTES / 2, &tm_V, &V_full[vs], 64, c * BN, zv);
+            ++vi;
+          }
+        }
+      }
+    producer_done:
+      // drain: the last issue of every stage must have landed before exit
+      for (uint32_t k = 0; k < 2 && k < di; ++k) {
+        const uint32_t i = di - 1 - k;
+        mbar_drain(&dO_full[i & 1], (i >> 1) & 1, err, 0x0111);
+      }
+      for (uint32_t k = 0; k < uint32_t(VST) && k < vi; ++k) {
+        const uint32_t i = vi - 1 - k;
+        mbar_drain(&V_full[i % VST], (i / VST) & 1, err, 0x0112);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------ P / mask producer
+    uint32_t pi = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int bhl = u / n_mb, mb = u - bhl * n_mb;
+      for (int pass = 0; pass < 2; ++pass) {
+        for (int c = 0; c < nchunks; ++c) {
+          const int ps = pi % PST;
+          if constexpr (!RAG) {
+            if (lane == 0) {
+              if (!mbar_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103)) goto pm_done;
+              mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
+              tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
+              tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
+            }
+          } else {
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) goto pm_done;
+            unsigned long long srcp[4], srcm[4];
+            uint32_t szp[4], szm[4], total = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int s = mb * BM + int(lane) + 32 * k;
+              szp[k] = szm[k] = 0;
+              srcp[k] = srcm[k] = 0;
+              if (s < sq) {
+                const unsigned long long el = ((unsigned long long)bhl * sq + s) * skv + (unsigned long long)c * BN;
+                srcp[k] = (el * 2) & ~15ull;
+                srcm[k] = el & ~15ull;
+                const unsigned long long rp = prm.p_end16 - srcp[k], rm = prm.m_end16 - srcm[k];
+                szp[k] = rp < (unsigned long long)C::P_PITCH ? uint32_t(rp) : uint32_t(C::P_PITCH);
+                szm[k] = rm < (unsigned long long)C::M_PITCH ? uint32_t(rm) : uint32_t(C::M_PITCH);
+                total += szp[k] + szm[k];
+              }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+            if (lane == 0) mbar_arrive_expect_tx(&PM_full[ps], total);
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int r = int(lane) + 32 * k;
+              if (szp[k]) {
+                bulk_load(smem + C::OFF_P + ps * C::P_BYTES + r * C::P_PITCH, prm.P + srcp[k], szp[k], &PM_full[ps]);
+                bulk_load(smem + C::OFF_M + ps * C::M_BYTES + r * C::M_PITCH, prm.M + srcm[k], szm[k], &PM_full[ps]);
+              }
+            }
+          }
+          ++pi;
+        }
+      }
+    }
+  pm_done:
+    if (lane == 0) {
+      for (uint32_t k = 0; k < uint32_t(PST) && k < pi; ++k) {
+        const uint32_t i = pi - 1 - k;
+        mbar_drain(&PM_full[i % PST], (i / PST) & 1, err, 0x0113);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+      uint32_t job = 0, vi = 0, di = 0;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const int db = di & 1;
+        if (!mbar_wait(&dO_full[db], (di >> 1) & 1, abort_flag, err, 0x0201)) goto mma_done;
+        const uint32_t a_base = smem_u32(smem + C::OFF_DO + db * DO_BYTES);
+        for (int pass = 0; pass < npass_mma; ++pass) {
+          for (int c = 0; c < nchunks; ++c) {
+            const int slot = job % TSLOTS;
+            if (!mbar_wait(&T_empty[slot], ((job / TSLOTS) & 1) ^ 1, abort_flag, err, 0x0202)) goto mma_done;
+            const int vs = vi % VST;
+            if (!mbar_wait(&V_full[vs], (vi / VST) & 1, abort_flag, err, 0x0203)) goto mma_done;
+            tc_fence_after();
+            const uint32_t b_base = smem_u32(smem + C::OFF_V + vs * V_BYTES);
+            const uint32_t d_tmem = tmem_base + slot * BN;
+#pragma unroll
+            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+              // 16 bf16 = 32 B step inside the 128 B swizzle atom; 64-column halves 16 KB / 8 KB apart
+              const uint32_t koff = (kk & 3) * 32;
+              const uint64_t ad = sdesc_sw128(a_base + (kk >> 2) * (DO_BYTES / 2) + koff, 16, 1024);
+              const uint64_t bd = sdesc_sw128(b_base + (kk >> 2) * (V_BYTES / 2) + koff, 16, 1024);
+              umma_bf16(d_tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&V_empty[vs]);
+            umma_commit(&T_full[slot]);
+            ++vi;
+            ++job;
+          }
+        }
+        umma_commit(&dO_empty[db]);
+        ++di;
+      }
+    mma_done:;
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t t_lane = uint32_t(q * 32) << 16;
+    const bool storer = (!RAG) && (warp == 4 && lane == 0);
+    const int use_mask = prm.use_mask;
+    const float scale = prm.scale;
+    const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
+    uint32_t job = 0, pi = 0, it = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int bhl = u / n_mb, mb = u - bhl * n_mb;
+      const int s_row = mb * BM + row;
+      const unsigned long long row_el = ((unsigned long long)bhl * sq + s_row) * skv;
+      const uint32_t job0 = job;
+      float acc = 0.f;
+      // ---- pass 1: row sums
+      for (int c = 0; c < nchunks; ++c) {
+        const int slot = job % TSLOTS;
+        if (!mbar_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0301)) goto epi_done;
+        tc_fence_after();
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + t_lane + slot * BN + half * 32, v);
+        tmem_wait_ld();
+        if (!resident) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&T_empty[slot]);
+        }
+        ++job;
+        const int ps = pi % PST;
+        if (!mbar_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) goto epi_done;
+        const unsigned long long el = row_el + (unsigned long long)c * BN;
+        uint32_t pw[16], mw[8];
+        load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES),
+                      row, half, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&PM_empty[ps]);
+        const int nvalid = RAG ? min(max(skv - (c * BN + half * 32), 0), 32) : 32;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float d = __uint_as_float(v[e]) * p_at(pw, e);
+          const bool keep = (!use_mask || m_at(mw, e)) && (!RAG || e < nvalid);
+          acc += keep ? d : 0.f;
+        }
+        ++pi;
+      }
+      // ---- combine the two column halves of each row
+      {
+        float* rxb = rx + (it & 1) * 2 * BM;
+        rxb[half * BM + row] = acc;
+        mbar_arrive(&pair_bar[q]);
+        if (!mbar_wait(&pair_bar[q], it & 1, abort_flag, err, 0x0303)) goto epi_done;
+        acc += rxb[(half ^ 1) * BM + row];
+      }
+      {
+        const float r = acc * scale;
+        // ---- pass 2: dS
+        for (int c = 0; c < nchunks; ++c) {
+          int slot;
+          if (resident) {
+            slot = (job0 + c) % TSLOTS;
+          } else {
+            slot = job % TSLOTS;
+            if (!mbar_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0304)) goto epi_done;
+            tc_fence_after();
+            ++job;
+          }
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(tmem_base + t_lane + slot * BN + half * 32, v);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&T_empty[slot]);
+          const int ps = pi % PST;
+          if (!mbar_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) goto epi_done;
+          const unsigned long long el = row_el + (unsigned long long)c * BN;
+          const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
+          uint32_t pw[16], mw[8];
+          load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, half, uint32_t(el * 2) & 15u,
+                        uint32_t(el) & 15u, pw, mw);
+          uint32_t o[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            float dp0 = __uint_as_float(v[2 * k]) * scale;
+            float dp1 = __uint_as_float(v[2 * k + 1]) * scale;
+            if (use_mask && !m_at(mw, 2 * k)) dp0 = 0.f;
+            if (use_mask && !m_at(mw, 2 * k + 1)) dp1 = 0.f;
+            const float p0 = p_at(pw, 2 * k), p1 = p_at(pw, 2 * k + 1);
+            o[k] = pack_bf16x2(p0 * (dp0 - r), p1 * (dp1 - r));
+          }
+          if constexpr (!RAG) {
+            // dS overwrites P in place (same swizzled positions), then one TMA store per chunk
+            const uint32_t p_row = p_stage + row * 128;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              sts128(p_row + (((half * 4 + i) ^ (row & 7)) << 4),
+                     make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dS_ready[ps]);
+            if (storer) {
+              if (!mbar_wait(&dS_ready[ps], (pi / PST) & 1, abort_flag, err, 0x0306)) goto epi_done;
+              tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
+              bulk_commit();
+              bulk_wait_read0();
+              mbar_arrive_cnt(&PM_empty[ps], 8);
+            }
+          } else {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&PM_empty[ps]);
+            // transpose through the warp's buffer: row-per-thread -> column-per-lane
+            const uint32_t srow = stg + lane * C::STG_PITCH;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              sts128(srow + i * 16, make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+            __syncwarp();
+            const int col = c * BN + half * 32 + int(lane);
+            const int rows_here = min(32, sq - (mb * BM + q * 32));
+            if (col < skv) {
+              unsigned short* dst = reinterpret_cast<unsigned short*>(prm.dS) +
+                                    ((unsigned long long)bhl * sq + mb * BM + q * 32) * skv + col;
+              for (int rr = 0; rr < rows_here; ++rr) {
+                unsigned short val;
+                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(val) : "r"(stg + rr * C::STG_PITCH + lane * 2));
+                dst[(unsigned long long)rr * skv] = val;
+              }
+            }
+            __syncwarp();
+          }
+          ++pi;
+        }
+      }
+      ++it;
+    }
+  epi_done:
+    if (storer) bulk_wait_all0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TSLOTS * BN);
+  }
+}
+
+}  // namespace ds
+}  // namespace attn_bwd

@@ -1,0 +1,326 @@
+// dv_kernel.cuh — fused dV kernel: dV[b,kvh] = Σ_{g<10} P_dropᵀ[b,10·kvh+g] · dO[b,:,10·kvh+g,:]
+// on tcgen05, with the sum over the 10 grouped query heads folded into the
+// K loop (K = 10 · seq_q), so no [bs,80,skv,128] expansion ever exists.
+//
+// Reference math: attn_bwd/starting_point.py:61-68 (dV_exp = P̃ᵀ·dO, then the
+// group sum and the bf16 cast).
+//
+// Work unit: one (batch, kv-head, 128-row tile of seq_kv).  Both operands are
+// MN-major in shared memory: A = P_drop tile [64 seq_q rows][128 seq_kv cols]
+// (seq_kv contiguous), B = dO tile [64 seq_q rows][128 d] read in place from
+// [bs, sq, 80, 128] (row stride 80·128·2 B).  The accumulator [128 x 128] f32
+// lives in TMEM, double-buffered across units so the epilogue of one unit
+// overlaps the MMAs of the next.
+//
+// Roles: warp 0 producer, warp 1 MMA issuer + TMEM owner, warps 2..5 epilogue
+// (warp w drains TMEM lanes 32·(w%4)..).
+//
+// Row formats (template flag RAG):
+//   RAG = false  seq_kv % 8 == 0: P_drop tiles are TMA tensor tiles (128B swizzle).
+//   RAG = true   any seq_kv: P_drop rows are not 16-byte aligned; the producer
+//                fetches each 128-column row segment with an untiled bulk copy
+//                from the 16-byte boundary below it into a padded row (272 B),
+//                and warps 6..9 re-align the bytes in registers and write the
+//                128B-swizzled MN-major tile the MMA reads (zeroing columns >=
+//                seq_kv and rows >= seq_q).
+#pragma once
+#include "sm100.cuh"
+
+namespace attn_bwd {
+namespace dv {
+constexpr int BM = 128;   // seq_kv rows per unit
+constexpr int BK = 64;    // seq_q rows per K chunk
+constexpr int A_BYTES = BK * BM * 2;          // 16 KB (two 64-col MN blocks of 8 KB)
+constexpr int B_BYTES = BK * kHeadDim * 2;    // 16 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+
+template <bool RAG>
+struct Cfg {
+  static constexpr int kThreads = RAG ? 320 : 192;
+  static constexpr int ST = RAG ? 4 : 6;               // operand stages
+  static constexpr int RST = RAG ? 4 : 0;              // raw P_drop row stages
+  static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack
+  static constexpr int RAW_BYTES = BK * RAW_PITCH;
+  static constexpr int OFF_RAW = ST * STAGE_BYTES;
+  static constexpr int OFF_BAR = OFF_RAW + RST * RAW_BYTES;
+  static constexpr int NBAR = 3 * ST + 2 * RST + 4;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024, "dV kernel shared memory");
+};
+
+struct Params {
+  int sq, skv;
+  int n_units;     // local (batch, kv-head) count × seq_kv tiles
+  int n_jt;        // seq_kv tiles per (batch, kv-head)
+  int n_kc;        // seq_q chunks per head
+  int unit_base;   // global (batch·8 + kv-head) index of local unit 0
+  int* err;
+  const uint8_t* Pd;              // local P_drop base (RAG path)
+  unsigned long long pd_end16;    // bytes of P_drop rounded up to 16
+};
+
+// out[j] = bytes [4j+sh, 4j+sh+4) of the little-endian stream `in` (NOUT+4 words).
+template <int NOUT>
+__device__ __forceinline__ void byte_shift(const uint32_t* in, uint32_t sh, uint32_t* out) {
+  uint32_t u[NOUT + 2], v[NOUT + 1];
+#pragma unroll
+  for (int j = 0; j < NOUT + 2; ++j) u[j] = (sh & 8) ? in[j + 2] : in[j];
+#pragma unroll
+  for (int j = 0; j < NOUT + 1; ++j) v[j] = (sh & 4) ? u[j + 1] : u[j];
+  const uint32_t bits = (sh & 3) * 8;
+#pragma unroll
+  for (int j = 0; j < NOUT; ++j) out[j] = __funnelshift_r(v[j], v[j + 1], bits);
+}
+
+template <bool RAG>
+__global__ void __launch_bounds__(Cfg<RAG>::kThreads, 1)
+dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  box (64,64,1) SW128
+          const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)         box (64,1,64,1) SW128
+          __nv_bfloat16* __restrict__ dV,              // local [units, skv, 128]
+          const Params prm) {
+  using namespace sm100;
+  using C = Cfg<RAG>;
+  constexpr int ST = C::ST, RST = C::RST;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + ST;
+  uint64_t* a_ready = bars + 2 * ST;      // RAG: the 4 re-align warps wrote the A tile
+  uint64_t* raw_full = a_ready + ST;
+  uint64_t* raw_empty = raw_full + RST;
+  uint64_t* acc_full = raw_empty + RST;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 4); }
+    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 4); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    if (!RAG) prefetch_tmap(&tm_Pd);
+    prefetch_tmap(&tm_dO);
+  }
+  if (warp == 1) { tmem_alloc(tmem_base_slot, 256); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+  const int n_units = prm.n_units, n_jt = prm.n_jt, n_kc = prm.n_kc;
+  int* err = prm.err;
+
+  if (warp == 0) {
+    uint32_t si = 0, ri = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int ul = u / n_jt, jt = u - ul * n_jt;
+      const int ug = prm.unit_base + ul;
+      const int b = ug / kKvHeads, kvh = ug - b * kKvHeads;
+      for (int g = 0; g < kGroups; ++g) {
+        const int h = kvh * kGroups + g;
+        const int bhl = ul * kGroups + g;
+        for (int kc = 0; kc < n_kc; ++kc) {
+          const int s = si % ST;
+          int ok = 1;
+          if (lane == 0) {
+            ok = mbar_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1101) ? 1 : 0;
+            if (ok) {
+              uint8_t* a = smem + s * STAGE_BYTES;
+              uint8_t* bsm = a + A_BYTES;
+              mbar_arrive_expect_tx(&full[s], RAG ? B_BYTES : STAGE_BYTES);
+              if (!RAG) {
+                tma_load_3d(a, &tm_Pd, &full[s], jt * BM, kc * BK, bhl);
+                tma_load_3d(a + A_BYTES / 2, &tm_Pd, &full[s], jt * BM + 64, kc * BK, bhl);
+              }
+              tma_load_4d(bsm, &tm_dO, &full[s], 0, h, kc * BK, b);
+              tma_load_4d(bsm + B_BYTES / 2, &tm_dO, &full[s], 64, h, kc * BK, b);
+            }
+          }
+          ++si;
+          if constexpr (RAG) {
+            const int rs = ri % RST;
+            if (lane == 0 && ok) ok = mbar_wait(&raw_empty[rs], ((ri / RST) & 1) ^ 1, abort_flag, err, 0x1102) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) goto prod_done;
+            unsigned long long src[2];
+            uint32_t sz[2], total = 0;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int srow = kc * BK + int(lane) + 32 * k;
+              sz[k] = 0;
+              src[k] = 0;
+              if (srow < prm.sq) {
+                const unsigned long long el =
+                    ((unsigned long long)bhl * prm.sq + srow) * prm.skv + (unsigned long long)jt * BM;
+                src[k] = (el * 2) & ~15ull;
+                const unsigned long long rem = prm.pd_end16 - src[k];
+                sz[k] = rem < (unsigned long long)C::RAW_PITCH ? uint32_t(rem) : uint32_t(C::RAW_PITCH);
+                total += sz[k];
+              }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+            if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], total);
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+              if (sz[k])
+                bulk_load(smem + C::OFF_RAW + rs * C::RAW_BYTES + (int(lane) + 32 * k) * C::RAW_PITCH, prm.Pd + src[k],
+                          sz[k], &raw_full[rs]);
+            ++ri;
+          } else {
+            if (!__shfl_sync(0xffffffffu, ok, 0)) goto prod_done;
+          }
+        }
+      }
+    }
+  prod_done:
+    if (lane == 0) {
+      for (uint32_t k = 0; k < uint32_t(ST) && k < si; ++k) {
+        const uint32_t i = si - 1 - k;
+        mbar_drain(&full[i % ST], (i / ST) & 1, err, 0x1111);
+      }
+      for (uint32_t k = 0; k < uint32_t(RST) && k < ri; ++k) {
+        const uint32_t i = ri - 1 - k;
+        mbar_drain(&raw_full[i % RST], (i / RST) & 1, err, 0x1112);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, kHeadDim, true, true);
+      uint32_t si = 0, ui = 0;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ui) {
+        const int acc = ui & 1;
+        if (!mbar_wait(&acc_empty[acc], ((ui >> 1) & 1) ^ 1, abort_flag, err, 0x1201)) goto mma_done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kHeadDim;
+        const int nk = kGroups * n_kc;
+        for (int k = 0; k < nk; ++k) {
+          const int s = si % ST;
+          if (!mbar_wait(&full[s], (si / ST) & 1, abort_flag, err, 0x1202)) goto mma_done;
+          if (RAG && !mbar_wait(&a_ready[s], (si / ST) & 1, abort_flag, err, 0x1203)) goto mma_done;
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t bsm = a + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // 16 k-rows = two 8-row swizzle atoms = 2048 B
+            const uint64_t ad = sdesc_sw128(a + kk * 2048, A_BYTES / 2, 1024);
+            const uint64_t bd = sdesc_sw128(bsm + kk * 2048, B_BYTES / 2, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (k > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          ++si;
+        }
+        umma_commit(&acc_full[acc]);
+      }
+    mma_done:;
+    }
+  } else if (warp < 6) {
+    // epilogue warps 2..5
+    const int q = warp & 3;
+    const uint32_t t_lane = uint32_t(q * 32) << 16;
+    const int skv = prm.skv;
+    uint32_t ui = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ui) {
+      const int ul = u / n_jt, jt = u - ul * n_jt;
+      const int acc = ui & 1;
+      if (!mbar_wait(&acc_full[acc], (ui >> 1) & 1, abort_flag, err, 0x1301)) break;
+      tc_fence_after();
+      const int j = jt * BM + q * 32 + lane;
+      __nv_bfloat16* out = dV + (size_t(ul) * skv + j) * kHeadDim;
+#pragma unroll
+      for (int cc = 0; cc < kHeadDim / 32; ++cc) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + t_lane + acc * kHeadDim + cc * 32, v);
+        tmem_wait_ld();
+        if (j < skv) {
+          uint4* o = reinterpret_cast<uint4*>(out + cc * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[i * 8 + 0]), __uint_as_float(v[i * 8 + 1]));
+            w.y = pack_bf16x2(__uint_as_float(v[i * 8 + 2]), __uint_as_float(v[i * 8 + 3]));
+            w.z = pack_bf16x2(__uint_as_float(v[i * 8 + 4]), __uint_as_float(v[i * 8 + 5]));
+            w.w = pack_bf16x2(__uint_as_float(v[i * 8 + 6]), __uint_as_float(v[i * 8 + 7]));
+            o[i] = w;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  else if (RAG) {
+    // re-align warps 6..9: thread t handles row r = t % 64 of the chunk and the
+    // 64-column MN block jb = t / 64
+    const int t = int(threadIdx.x) - 6 * 32;
+    const int r = t & 63, jb = t >> 6;
+    const int sq = prm.sq, skv = prm.skv;
+    uint32_t si = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int ul = u / n_jt, jt = u - ul * n_jt;
+      const int nvalid = min(max(skv - (jt * BM + jb * 64), 0), 64);
+      for (int g = 0; g < kGroups; ++g) {
+        const int bhl = ul * kGroups + g;
+        for (int kc = 0; kc < n_kc; ++kc, ++si) {
+          const int s = si % ST, rs = si % RST;
+          if (!mbar_wait(&raw_full[rs], (si / RST) & 1, abort_flag, err, 0x1401)) goto realign_done;
+          if (!mbar_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1402)) goto realign_done;
+          const int srow = kc * BK + r;
+          uint32_t w[32];
+          if (srow < sq) {
+            const unsigned long long el = ((unsigned long long)bhl * sq + srow) * skv + (unsigned long long)jt * BM;
+            const uint32_t src = smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES + r * C::RAW_PITCH + jb * 128);
+            uint32_t in[36];
+#pragma unroll
+            for (int i = 0; i < 9; ++i) {
+              const uint4 x = lds128(src + i * 16);
+              in[4 * i] = x.x; in[4 * i + 1] = x.y; in[4 * i + 2] = x.z; in[4 * i + 3] = x.w;
+            }
+            byte_shift<32>(in, uint32_t(el * 2) & 15u, w);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              if (2 * k >= nvalid) w[k] = 0;
+              else if (2 * k + 1 >= nvalid) w[k] &= 0xFFFFu;
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) w[k] = 0;
+          }
+          // 128B-swizzled MN-major row: 16-byte chunk k of row r sits at chunk k ^ (r % 8)
+          const uint32_t dst = smem_u32(smem + s * STAGE_BYTES + jb * (A_BYTES / 2) + r * 128);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            sts128(dst + ((k ^ (r & 7)) << 4), make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&raw_empty[rs]);
+            mbar_arrive(&a_ready[s]);
+          }
+        }
+      }
+    }
+  realign_done:;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 256);
+  }
+}
+
+}  // namespace dv
+}  // namespace attn_bwd

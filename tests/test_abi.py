@@ -1,0 +1,60 @@
+"""The C-ABI library: builds, loads without a GPU, exports every declared symbol,
+and rejects bad arguments before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from attn_bwd_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include")) if f.endswith(".h")]
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(attn_bwd_b200\w*)\s*\(", src, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_built_in_tree():
+    assert os.path.exists(_lib.LIB_PATH), "run __graft_entry__.build() first"
+
+
+def test_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert {"attn_bwd_b200", "attn_bwd_b200_shard", "attn_bwd_b200_poll_error"} <= names
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/ but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_strerror_and_version():
+    lib = _lib.load()
+    assert lib.attn_bwd_b200_version() >= 100
+    for code in range(8):
+        assert len(_lib.strerror(code)) > 0
+    assert _lib.strerror(99) == "unknown error"
+
+
+@pytest.mark.parametrize("bs,sq,skv", [(-1, 4, 4), (1, -4, 4), (1, 4, -4)])
+def test_negative_sizes_rejected_without_device(bs, sq, skv):
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    rc = lib.attn_bwd_b200(nul, nul, nul, nul, nul, 0.1, bs, sq, skv, nul, nul, nul)
+    assert rc == _lib.EINVAL
+
+
+def test_bad_unit_range_rejected_without_device():
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    rc = lib.attn_bwd_b200_shard(nul, nul, nul, nul, nul, 0.1, 2, 4, 16, 3, 17, nul, nul, nul)
+    assert rc == _lib.EINVAL
+    rc = lib.attn_bwd_b200_dv_shard(nul, nul, 2, 4, 16, 5, 4, nul, nul)
+    assert rc == _lib.EINVAL

@@ -1,0 +1,154 @@
+"""Parity of the CUDA path (through the C-ABI) with the CPU oracle.
+
+Tolerance is the reference's own check (eval_modal_attn_bwd.py:173-197):
+torch.allclose(ref.float(), out.float(), rtol=1e-2, atol=1e-2) for dS and dV.
+"""
+import pytest
+import torch
+
+import attn_bwd_b200 as ab
+from attn_bwd_b200.generate import generate_input, generate_input_lowmem
+from golden_io import CASES, load_case
+from oracle.attn_bwd_oracle import attn_bwd_reference, attn_bwd_units
+
+pytestmark = pytest.mark.gpu
+RTOL = ATOL = 1e-2
+
+CONFIGS = {  # BASELINE.json configs c0..c4
+    "c0": (2, 64, 96), "c1": (6, 384, 384), "c2": (12, 301, 467),
+    "c3": (2, 2048, 3072), "c4": (48, 640, 640),
+}
+# SOL-ExecBench shapes (eval_modal_attn_bwd.py:18-35), sizes only
+SOL_SHAPES = [(4, 256, 256), (8, 373, 449), (4, 1024, 2048), (64, 128, 128), (2, 256, 512),
+              (32, 691, 773), (8, 128, 128), (32, 512, 512), (4, 211, 293), (8, 256, 256),
+              (16, 128, 256), (1, 1024, 1024), (16, 256, 512), (32, 128, 128), (1, 512, 512),
+              (1, 4096, 4096)]
+
+
+def _close(name, ref, out):
+    ok = torch.allclose(ref.float(), out.float().cpu(), rtol=RTOL, atol=ATOL)
+    if not ok:
+        d = (ref.float() - out.float().cpu()).abs()
+        raise AssertionError(f"{name} mismatch: max={d.max().item():.4e} mean={d.mean().item():.4e}")
+
+
+def _to(data, dev):
+    return tuple(t.to(dev) if isinstance(t, torch.Tensor) else t for t in data)
+
+
+def _check_full(data_cpu, dev):
+    data = _to(data_cpu, dev)
+    dS, dV = ab.custom_kernel(data)
+    torch.cuda.synchronize()
+    assert ab.poll_error() == 0
+    rS, rV = attn_bwd_reference(data_cpu)
+    assert dS.shape == rS.shape and dV.shape == rV.shape
+    assert dS.dtype == torch.bfloat16 and dV.dtype == torch.bfloat16
+    _close("grad_attn_scores", rS, dS)
+    _close("grad_value_states", rV, dV)
+
+
+def _check_sampled(data, units):
+    """data on the GPU; compares the listed units with the per-unit oracle."""
+    dS, dV = ab.custom_kernel(data)
+    torch.cuda.synchronize()
+    assert ab.poll_error() == 0
+    ref = attn_bwd_units(data, units)
+    for u in units:
+        b, kvh = divmod(u, 8)
+        _close(f"dS unit {u}", ref[u][0], dS[b, kvh * 10:kvh * 10 + 10])
+        _close(f"dV unit {u}", ref[u][1], dV[b, kvh])
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_golden(name, cuda):
+    data, rS, rV, _ = load_case(name)
+    dS, dV = ab.custom_kernel(_to(data, cuda))
+    torch.cuda.synchronize()
+    _close("grad_attn_scores", rS, dS)
+    _close("grad_value_states", rV, dV)
+
+
+@pytest.mark.parametrize("cfg", ["c0", "c1"])
+def test_config_full_oracle(cfg, cuda):
+    bs, sq, skv = CONFIGS[cfg]
+    _check_full(generate_input(bs, sq, skv, 1000 + int(cfg[1])), cuda)
+
+
+@pytest.mark.parametrize("cfg", ["c2", "c3", "c4"])
+def test_config_sampled_units(cfg, cuda):
+    bs, sq, skv = CONFIGS[cfg]
+    data = generate_input_lowmem(bs, sq, skv, 1000 + int(cfg[1]), device=cuda)
+    n = bs * 8
+    units = sorted({0, 1, 7, n // 2, n - 1})
+    _check_sampled(data, units)
+
+
+@pytest.mark.parametrize("shape", SOL_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_sol_shapes_sampled(shape, cuda):
+    bs, sq, skv = shape
+    seed = 1001 + SOL_SHAPES.index(shape)
+    data = generate_input_lowmem(bs, sq, skv, seed, device=cuda)
+    n = bs * 8
+    _check_sampled(data, sorted({0, n // 3, n - 1}))
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 16), (1, 1, 1), (1, 3, 1), (1, 127, 48), (1, 129, 64),
+                                   (2, 64, 272), (1, 200, 512), (1, 17, 528), (1, 64, 40)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_edge_shapes(shape, cuda):
+    bs, sq, skv = shape
+    _check_full(generate_input(bs, sq, skv, 77), cuda)
+
+
+@pytest.mark.parametrize("p", [0.0, 0.3, -0.5])
+def test_dropout_values(p, cuda):
+    _check_full(generate_input(1, 64, 128, 5, dropout_p=max(p, 0.0))[:5] + (p,), cuda)
+
+
+def test_empty_seq_q(cuda):
+    data = _to(generate_input(1, 0, 32, 3), cuda)
+    dS, dV = ab.custom_kernel(data)
+    assert dS.shape == (1, 80, 0, 32)
+    assert torch.count_nonzero(dV).item() == 0
+
+
+def test_noncontiguous_inputs(cuda):
+    data_cpu = generate_input(1, 32, 64, 9)
+    data = list(_to(data_cpu, cuda))
+    data[0] = data[0].transpose(1, 2).contiguous().transpose(1, 2)    # same values, other strides
+    dS, dV = ab.custom_kernel(tuple(data))
+    rS, rV = attn_bwd_reference(data_cpu)
+    _close("dS", rS, dS)
+    _close("dV", rV, dV)
+
+
+def test_repeat_calls_deterministic(cuda):
+    data = _to(generate_input(2, 130, 192, 4), cuda)
+    a = ab.custom_kernel(data)
+    b = ab.custom_kernel(data)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+def test_shard_calls_match_full(cuda):
+    bs, sq, skv = 2, 96, 128
+    data = _to(generate_input(bs, sq, skv, 21), cuda)
+    dS, dV = ab.custom_kernel(data)
+    dO, P, Pd, V, M, p = data
+    for u0, u1 in [(0, 3), (3, 11), (11, 16)]:
+        h0, h1 = u0 * 10, u1 * 10
+        sl = lambda t: t.reshape(bs * 80, sq, skv)[h0:h1]
+        sS, sV = ab.attn_bwd_shard((dO, sl(P), sl(Pd), V, sl(M), p), u0, u1)
+        assert torch.equal(sS, dS.reshape(bs * 80, sq, skv)[h0:h1])
+        assert torch.equal(sV, dV.reshape(bs * 8, skv, 128)[u0:u1])
+
+
+def test_current_stream_ordering(cuda):
+    data = _to(generate_input(1, 256, 256, 6), cuda)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        dS, dV = ab.custom_kernel(data)
+    s.synchronize()
+    rS, rV = attn_bwd_reference(_to(data, "cpu"))
+    _close("dS", rS, dS)
+    _close("dV", rV, dV)
