@@ -216,34 +216,38 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   int* err = prm.err;
 
   if (warp == 0) {
-    // ------------------------------------------------ dO / V producer
-    if (lane == 0) {
-      uint32_t vi = 0, di = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const int bhl = u / n_mb, mb = u - bhl * n_mb;
-        const int bh = prm.bh_base + bhl;
-        const int b = bh / kHeads, h = bh - b * kHeads;
-        const int zv = b * kKvHeads + h / kGroups;
-        const int db = di & 1;
-        if (!mbar_wait(&dO_empty[db], ((di >> 1) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
+    // ------------------------------------------------ dO / V producer (lane 0 issues)
+    uint32_t vi = 0, di = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int bhl = u / n_mb, mb = u - bhl * n_mb;
+      const int bh = prm.bh_base + bhl;
+      const int b = bh / kHeads, h = bh - b * kHeads;
+      const int zv = b * kKvHeads + h / kGroups;
+      const int db = di & 1;
+      if (!warp_wait(&dO_empty[db], ((di >> 1) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
+      if (lane == 0) {
         mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
         tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
         tma_load_4d(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
-        ++di;
-        for (int pass = 0; pass < npass_mma; ++pass) {
-          for (int c = 0; c < nchunks; ++c) {
-            const int vs = vi % VST;
-            if (!mbar_wait(&V_empty[vs], ((vi / VST) & 1) ^ 1, abort_flag, err, 0x0102)) goto producer_done;
+      }
+      ++di;
+      for (int pass = 0; pass < npass_mma; ++pass) {
+        for (int c = 0; c < nchunks; ++c) {
+          const int vs = vi % VST;
+          if (!warp_wait(&V_empty[vs], ((vi / VST) & 1) ^ 1, abort_flag, err, 0x0102)) goto producer_done;
+          if (lane == 0) {
             mbar_arrive_expect_tx(&V_full[vs], V_BYTES);
             uint8_t* dst = smem + C::OFF_V + vs * V_BYTES;
             tma_load_3d(dst, &tm_V, &V_full[vs], 0, c * BN, zv);
             tma_load_3d(dst + V_BYTES / 2, &tm_V, &V_full[vs], 64, c * BN, zv);
-            ++vi;
           }
+          ++vi;
         }
       }
-    producer_done:
-      // drain: the last issue of every stage must have landed before exit
+    }
+  producer_done:
+    // drain: the last issue of every stage must have landed before exit
+    if (lane == 0) {
       for (uint32_t k = 0; k < 2 && k < di; ++k) {
         const uint32_t i = di - 1 - k;
         mbar_drain(&dO_full[i & 1], (i >> 1) & 1, err, 0x0111);
@@ -253,6 +257,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         mbar_drain(&V_full[i % VST], (i / VST) & 1, err, 0x0112);
       }
     }
+    __syncwarp();
   } else if (warp == 2) {
     // ------------------------------------------------ P / mask producer
     uint32_t pi = 0;
@@ -261,18 +266,14 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       for (int pass = 0; pass < 2; ++pass) {
         for (int c = 0; c < nchunks; ++c) {
           const int ps = pi % PST;
+          if (!warp_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103)) goto pm_done;
           if constexpr (!RAG) {
             if (lane == 0) {
-              if (!mbar_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103)) goto pm_done;
               mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
               tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
               tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
             }
           } else {
-            int ok = 1;
-            if (lane == 0) ok = mbar_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103) ? 1 : 0;
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) goto pm_done;
             unsigned long long srcp[4], srcm[4];
             uint32_t szp[4], szm[4], total = 0;
 #pragma unroll
@@ -314,22 +315,23 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         mbar_drain(&PM_full[i % PST], (i / PST) & 1, err, 0x0113);
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
-      uint32_t job = 0, vi = 0, di = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const int db = di & 1;
-        if (!mbar_wait(&dO_full[db], (di >> 1) & 1, abort_flag, err, 0x0201)) goto mma_done;
-        const uint32_t a_base = smem_u32(smem + C::OFF_DO + db * DO_BYTES);
-        for (int pass = 0; pass < npass_mma; ++pass) {
-          for (int c = 0; c < nchunks; ++c) {
-            const int slot = job % TSLOTS;
-            if (!mbar_wait(&T_empty[slot], ((job / TSLOTS) & 1) ^ 1, abort_flag, err, 0x0202)) goto mma_done;
-            const int vs = vi % VST;
-            if (!mbar_wait(&V_full[vs], (vi / VST) & 1, abort_flag, err, 0x0203)) goto mma_done;
-            tc_fence_after();
+    // ------------------------------------------------ MMA issuer (lane 0 issues)
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+    uint32_t job = 0, vi = 0, di = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int db = di & 1;
+      if (!warp_wait(&dO_full[db], (di >> 1) & 1, abort_flag, err, 0x0201)) goto mma_done;
+      const uint32_t a_base = smem_u32(smem + C::OFF_DO + db * DO_BYTES);
+      for (int pass = 0; pass < npass_mma; ++pass) {
+        for (int c = 0; c < nchunks; ++c) {
+          const int slot = job % TSLOTS;
+          if (!warp_wait(&T_empty[slot], ((job / TSLOTS) & 1) ^ 1, abort_flag, err, 0x0202)) goto mma_done;
+          const int vs = vi % VST;
+          if (!warp_wait(&V_full[vs], (vi / VST) & 1, abort_flag, err, 0x0203)) goto mma_done;
+          tc_fence_after();
+          if (lane == 0) {
             const uint32_t b_base = smem_u32(smem + C::OFF_V + vs * V_BYTES);
             const uint32_t d_tmem = tmem_base + slot * BN;
 #pragma unroll
@@ -342,15 +344,17 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
             }
             umma_commit(&V_empty[vs]);
             umma_commit(&T_full[slot]);
-            ++vi;
-            ++job;
           }
+          __syncwarp();
+          ++vi;
+          ++job;
         }
-        umma_commit(&dO_empty[db]);
-        ++di;
       }
-    mma_done:;
+      if (lane == 0) umma_commit(&dO_empty[db]);
+      __syncwarp();
+      ++di;
     }
+  mma_done:;
   } else if (warp >= 4) {
     // ------------------------------------------------ epilogue
     const int q = warp & 3;
@@ -361,7 +365,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     const int use_mask = prm.use_mask;
     const float scale = prm.scale;
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
-    uint32_t job = 0, pi = 0, it = 0;
+    uint32_t job = 0, pi = 0, it = 0, dsr_par = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       const int s_row = mb * BM + row;
@@ -371,7 +375,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       // ---- pass 1: row sums
       for (int c = 0; c < nchunks; ++c) {
         const int slot = job % TSLOTS;
-        if (!mbar_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0301)) goto epi_done;
+        if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0301)) goto epi_done;
         tc_fence_after();
         uint32_t v[32];
         __syncwarp();
@@ -384,7 +388,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         }
         ++job;
         const int ps = pi % PST;
-        if (!mbar_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) goto epi_done;
+        if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) goto epi_done;
         const unsigned long long el = row_el + (unsigned long long)c * BN;
         uint32_t pw[16], mw[8];
         load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES),
@@ -405,7 +409,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         float* rxb = rx + (it & 1) * 2 * BM;
         rxb[half * BM + row] = acc;
         mbar_arrive(&pair_bar[q]);
-        if (!mbar_wait(&pair_bar[q], it & 1, abort_flag, err, 0x0303)) goto epi_done;
+        if (!warp_wait(&pair_bar[q], it & 1, abort_flag, err, 0x0303)) goto epi_done;
         acc += rxb[(half ^ 1) * BM + row];
       }
       {
@@ -417,7 +421,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
             slot = (job0 + c) % TSLOTS;
           } else {
             slot = job % TSLOTS;
-            if (!mbar_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0304)) goto epi_done;
+            if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0304)) goto epi_done;
             tc_fence_after();
             ++job;
           }
@@ -429,7 +433,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           __syncwarp();
           if (lane == 0) mbar_arrive(&T_empty[slot]);
           const int ps = pi % PST;
-          if (!mbar_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) goto epi_done;
+          if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) goto epi_done;
           const unsigned long long el = row_el + (unsigned long long)c * BN;
           const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
           uint32_t pw[16], mw[8];
@@ -455,12 +459,20 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&dS_ready[ps]);
-            if (storer) {
-              if (!mbar_wait(&dS_ready[ps], (pi / PST) & 1, abort_flag, err, 0x0306)) goto epi_done;
-              tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
-              bulk_commit();
-              bulk_wait_read0();
-              mbar_arrive_cnt(&PM_empty[ps], 8);
+            if (warp == 4) {
+              // dS_ready[ps] completes once per pass-2 use of stage ps; its parity is tracked here
+              int ok = 1;
+              if (lane == 0) {
+                ok = mbar_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306) ? 1 : 0;
+                dsr_par ^= 1u << ps;
+                if (ok) {
+                  tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
+                  bulk_commit();
+                  bulk_wait_read0();
+                  mbar_arrive_cnt(&PM_empty[ps], 8);
+                }
+              }
+              if (!__shfl_sync(0xffffffffu, ok, 0)) goto epi_done;
             }
           } else {
             __syncwarp();
@@ -491,6 +503,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     }
   epi_done:
     if (storer) bulk_wait_all0();
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -126,10 +126,9 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
         const int bhl = ul * kGroups + g;
         for (int kc = 0; kc < n_kc; ++kc) {
           const int s = si % ST;
-          int ok = 1;
+          if (!warp_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1101)) goto prod_done;
           if (lane == 0) {
-            ok = mbar_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1101) ? 1 : 0;
-            if (ok) {
+            {
               uint8_t* a = smem + s * STAGE_BYTES;
               uint8_t* bsm = a + A_BYTES;
               mbar_arrive_expect_tx(&full[s], RAG ? B_BYTES : STAGE_BYTES);
@@ -144,9 +143,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
           ++si;
           if constexpr (RAG) {
             const int rs = ri % RST;
-            if (lane == 0 && ok) ok = mbar_wait(&raw_empty[rs], ((ri / RST) & 1) ^ 1, abort_flag, err, 0x1102) ? 1 : 0;
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) goto prod_done;
+            if (!warp_wait(&raw_empty[rs], ((ri / RST) & 1) ^ 1, abort_flag, err, 0x1102)) goto prod_done;
             unsigned long long src[2];
             uint32_t sz[2], total = 0;
 #pragma unroll
@@ -173,8 +170,6 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
                 bulk_load(smem + C::OFF_RAW + rs * C::RAW_BYTES + (int(lane) + 32 * k) * C::RAW_PITCH, prm.Pd + src[k],
                           sz[k], &raw_full[rs]);
             ++ri;
-          } else {
-            if (!__shfl_sync(0xffffffffu, ok, 0)) goto prod_done;
           }
         }
       }
@@ -190,37 +185,42 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
         mbar_drain(&raw_full[i % RST], (i / RST) & 1, err, 0x1112);
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, kHeadDim, true, true);
-      uint32_t si = 0, ui = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ui) {
-        const int acc = ui & 1;
-        if (!mbar_wait(&acc_empty[acc], ((ui >> 1) & 1) ^ 1, abort_flag, err, 0x1201)) goto mma_done;
-        tc_fence_after();
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, kHeadDim, true, true);
+    uint32_t si = 0, ui = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ui) {
+      const int acc = ui & 1;
+      if (!warp_wait(&acc_empty[acc], ((ui >> 1) & 1) ^ 1, abort_flag, err, 0x1201)) goto mma_done;
+      tc_fence_after();
+      {
         const uint32_t d_tmem = tmem_base + acc * kHeadDim;
         const int nk = kGroups * n_kc;
         for (int k = 0; k < nk; ++k) {
           const int s = si % ST;
-          if (!mbar_wait(&full[s], (si / ST) & 1, abort_flag, err, 0x1202)) goto mma_done;
-          if (RAG && !mbar_wait(&a_ready[s], (si / ST) & 1, abort_flag, err, 0x1203)) goto mma_done;
+          if (!warp_wait(&full[s], (si / ST) & 1, abort_flag, err, 0x1202)) goto mma_done;
+          if (RAG && !warp_wait(&a_ready[s], (si / ST) & 1, abort_flag, err, 0x1203)) goto mma_done;
           tc_fence_after();
-          const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t bsm = a + A_BYTES;
+          if (lane == 0) {
+            const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
+            const uint32_t bsm = a + A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            // 16 k-rows = two 8-row swizzle atoms = 2048 B
-            const uint64_t ad = sdesc_sw128(a + kk * 2048, A_BYTES / 2, 1024);
-            const uint64_t bd = sdesc_sw128(bsm + kk * 2048, B_BYTES / 2, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (k > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              // 16 k-rows = two 8-row swizzle atoms = 2048 B
+              const uint64_t ad = sdesc_sw128(a + kk * 2048, A_BYTES / 2, 1024);
+              const uint64_t bd = sdesc_sw128(bsm + kk * 2048, B_BYTES / 2, 1024);
+              umma_bf16(d_tmem, ad, bd, idesc, (k > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&empty[s]);
           }
-          umma_commit(&empty[s]);
+          __syncwarp();
           ++si;
         }
-        umma_commit(&acc_full[acc]);
+        if (lane == 0) umma_commit(&acc_full[acc]);
+        __syncwarp();
       }
-    mma_done:;
     }
+  mma_done:;
   } else if (warp < 6) {
     // epilogue warps 2..5
     const int q = warp & 3;
@@ -230,7 +230,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ui) {
       const int ul = u / n_jt, jt = u - ul * n_jt;
       const int acc = ui & 1;
-      if (!mbar_wait(&acc_full[acc], (ui >> 1) & 1, abort_flag, err, 0x1301)) break;
+      if (!warp_wait(&acc_full[acc], (ui >> 1) & 1, abort_flag, err, 0x1301)) break;
       tc_fence_after();
       const int j = jt * BM + q * 32 + lane;
       __nv_bfloat16* out = dV + (size_t(ul) * skv + j) * kHeadDim;
@@ -273,8 +273,8 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
         const int bhl = ul * kGroups + g;
         for (int kc = 0; kc < n_kc; ++kc, ++si) {
           const int s = si % ST, rs = si % RST;
-          if (!mbar_wait(&raw_full[rs], (si / RST) & 1, abort_flag, err, 0x1401)) goto realign_done;
-          if (!mbar_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1402)) goto realign_done;
+          if (!warp_wait(&raw_full[rs], (si / RST) & 1, abort_flag, err, 0x1401)) goto realign_done;
+          if (!warp_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1402)) goto realign_done;
           const int srow = kc * BK + r;
           uint32_t w[32];
           if (srow < sq) {

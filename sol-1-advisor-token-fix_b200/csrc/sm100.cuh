@@ -93,6 +93,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return true;
 }
 
+// Warp-uniform bounded wait: all 32 lanes poll (each gets the barrier's acquire
+// ordering) and the outcome is agreed with a vote, so on a timeout the whole
+// warp leaves together and no lane is left behind in a __syncwarp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                          int code) {
+  const bool ok = mbar_wait(bar, parity, abort, err, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Drain wait used on the way out of a producer: waits (bounded, ignoring the
 // abort flag) for a phase of copies this thread issued, so no TMA write can
 // land in shared memory after the CTA has exited.
