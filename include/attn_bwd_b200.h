@@ -76,6 +76,13 @@ int attn_bwd_b200_dv_shard(const void* grad_attn_output, const void* attn_weight
  * evaluator has no counterpart; it reports exceptions (eval_modal_attn_bwd.py:294-302). */
 int attn_bwd_b200_poll_error(void);
 
+/* Self-test of failure detection (no reference counterpart): launches one warp
+ * that waits on a barrier nothing will complete, with a limit of limit_us
+ * microseconds (1..1000000).  The wait gives up, records code 0x7001 for
+ * attn_bwd_b200_poll_error and the kernel exits; the context stays usable.
+ * No GPU fault, trap or hang is involved. */
+int attn_bwd_b200_selftest_wait_timeout(int limit_us, attn_bwd_stream_t stream);
+
 /* Human-readable text for an ATTN_BWD_E* code (static storage). */
 const char* attn_bwd_b200_strerror(int code);
 

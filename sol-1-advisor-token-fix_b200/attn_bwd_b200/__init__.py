@@ -81,11 +81,11 @@ def _check_inputs(data, u0=None, u1=None):
     dO = _prep(dO, "grad_attn_output", torch.bfloat16, (bs, sq, NUM_ATTENTION_HEADS, HEAD_DIM))
     V = _prep(V, "value_states", torch.bfloat16, (bs, NUM_KEY_VALUE_HEADS, skv, HEAD_DIM))
     if P is not None:
-        P = _prep(P, "attn_weights", torch.bfloat16, sshape, flexible=not full)
+        P = _prep(P, "attn_weights", torch.bfloat16, sshape, flexible=True)
     if Pd is not None:
-        Pd = _prep(Pd, "attn_weights_dropped", torch.bfloat16, sshape, flexible=not full)
+        Pd = _prep(Pd, "attn_weights_dropped", torch.bfloat16, sshape, flexible=True)
     if M is not None:
-        M = _prep(M, "dropout_mask", torch.bool, sshape, flexible=not full)
+        M = _prep(M, "dropout_mask", torch.bool, sshape, flexible=True)
     devs = {t.device for t in (dO, P, Pd, V, M) if t is not None}
     if len(devs) != 1:
         raise ValueError(f"all tensors must be on one CUDA device, got {devs}")

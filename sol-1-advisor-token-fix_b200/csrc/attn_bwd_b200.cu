@@ -82,7 +82,14 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 struct Shape {
   int bs, sq, skv, u0, u1;
   int n_units() const { return u1 - u0; }
+  // element counts of the shard's tensors (a null pointer is accepted only for an empty one)
+  long long n_scores() const { return (long long)n_units() * kGroups * sq * skv; }
+  long long n_dO() const { return (long long)bs * sq * kHeads * kHeadDim; }
+  long long n_V() const { return (long long)bs * kKvHeads * skv * kHeadDim; }
+  long long n_dV() const { return (long long)n_units() * skv * kHeadDim; }
 };
+
+inline bool ptr_ok(const void* p, long long n) { return p != nullptr || n == 0; }
 
 int check_shape(const Shape& s) {
   if (s.bs < 0 || s.sq < 0 || s.skv < 0) return ATTN_BWD_EINVAL;
@@ -201,6 +208,22 @@ int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void*
   return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 
+// Self-test of the bounded-wait machinery: one warp waits on an mbarrier that
+// nothing will ever arrive on, with a limit of `limit_ns`.  The wait must give
+// up, record `code` in the error flag and let the kernel exit normally.
+__global__ void wait_timeout_selftest(int* err, int code, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    abort_flag = 0;
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  const bool ok = sm100::mbar_wait(&bar, 0, &abort_flag, err, code, limit_ns);
+  (void)__all_sync(0xffffffffu, ok);
+}
+
 int prologue(DeviceState** st, const Shape& s) {
   int rc = check_shape(s);
   if (rc) return rc;
@@ -217,7 +240,9 @@ int attn_bwd_b200_ds_shard(const void* dO, const void* P, const void* V, const u
   DeviceState* st = nullptr;
   int rc = prologue(&st, s);
   if (rc) return rc;
-  if (!dO || !P || !V || !M || !dS) return s.n_units() == 0 ? ATTN_BWD_OK : ATTN_BWD_EINVAL;
+  if (!ptr_ok(dO, s.n_dO()) || !ptr_ok(P, s.n_scores()) || !ptr_ok(V, s.n_V()) || !ptr_ok(M, s.n_scores()) ||
+      !ptr_ok(dS, s.n_scores()))
+    return ATTN_BWD_EINVAL;
   if (!aligned16(dO) || !aligned16(P) || !aligned16(V) || !aligned16(M) || !aligned16(dS)) return ATTN_BWD_EALIGN;
   return launch_ds(*st, s, dO, P, V, M, p, dS, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -228,7 +253,7 @@ int attn_bwd_b200_dv_shard(const void* dO, const void* Pd, int bs, int sq, int s
   DeviceState* st = nullptr;
   int rc = prologue(&st, s);
   if (rc) return rc;
-  if (!dO || !Pd || !dV) return s.n_units() == 0 ? ATTN_BWD_OK : ATTN_BWD_EINVAL;
+  if (!ptr_ok(dO, s.n_dO()) || !ptr_ok(Pd, s.n_scores()) || !ptr_ok(dV, s.n_dV())) return ATTN_BWD_EINVAL;
   if (!aligned16(dO) || !aligned16(Pd) || !aligned16(dV)) return ATTN_BWD_EALIGN;
   return launch_dv(*st, s, dO, Pd, dV, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -239,7 +264,9 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
   DeviceState* st = nullptr;
   int rc = prologue(&st, s);
   if (rc) return rc;
-  if (!dO || !P || !Pd || !V || !M || !dS || !dV) return s.n_units() == 0 ? ATTN_BWD_OK : ATTN_BWD_EINVAL;
+  if (!ptr_ok(dO, s.n_dO()) || !ptr_ok(P, s.n_scores()) || !ptr_ok(Pd, s.n_scores()) || !ptr_ok(V, s.n_V()) ||
+      !ptr_ok(M, s.n_scores()) || !ptr_ok(dS, s.n_scores()) || !ptr_ok(dV, s.n_dV()))
+    return ATTN_BWD_EINVAL;
   if (!aligned16(dO) || !aligned16(P) || !aligned16(Pd) || !aligned16(V) || !aligned16(M) || !aligned16(dS) ||
       !aligned16(dV))
     return ATTN_BWD_EALIGN;
@@ -252,6 +279,16 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
 int attn_bwd_b200(const void* dO, const void* P, const void* Pd, const void* V, const uint8_t* M, float p, int bs,
                   int sq, int skv, void* dS, void* dV, attn_bwd_stream_t stream) {
   return attn_bwd_b200_shard(dO, P, Pd, V, M, p, bs, sq, skv, 0, bs * kKvHeads, dS, dV, stream);
+}
+
+int attn_bwd_b200_selftest_wait_timeout(int limit_us, attn_bwd_stream_t stream) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  if (limit_us <= 0 || limit_us > 1000000) return ATTN_BWD_EINVAL;
+  wait_timeout_selftest<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      st->err, 0x7001, (unsigned long long)limit_us * 1000ull);
+  return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 
 int attn_bwd_b200_poll_error(void) {

@@ -78,13 +78,13 @@ __device__ __forceinline__ uint64_t global_ns() {
 // microseconds at most.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* err, int code) {
+                                          int* err, int code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   uint32_t n = 0;
   while (!mbar_try_wait(bar, parity)) {
     if (*abort) return false;
-    if ((++n & 31u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+    if ((++n & 31u) == 0 && global_ns() - t0 > limit_ns) {
       raise_error(err, code);
       *abort = 1;
       return false;

@@ -152,3 +152,16 @@ def test_current_stream_ordering(cuda):
     rS, rV = attn_bwd_reference(_to(data, "cpu"))
     _close("dS", rS, dS)
     _close("dV", rV, dV)
+
+
+def test_bounded_wait_reports_and_recovers(cuda):
+    """A kernel wait that can never complete gives up after its limit, the error
+    is reported through the C-ABI, and the next real call still works."""
+    import ctypes
+    from attn_bwd_b200 import _lib
+    assert ab.poll_error() == 0
+    _lib.call("attn_bwd_b200_selftest_wait_timeout", 20000,
+              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert ab.poll_error() == 0x7001
+    assert ab.poll_error() == 0          # cleared by the poll
+    _check_full(generate_input(1, 16, 64, 8), cuda)
