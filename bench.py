@@ -154,7 +154,7 @@ def max_over_ranks(x, world):
     return t.item()
 
 
-def cpu_sample(cfg, units_target_s=12.0, max_units=64):
+def cpu_sample(cfg, units_target_s=12.0, max_units=100000):
     """Times the CPU oracle on whole (batch, kv-head) units of the config until
     about `units_target_s` seconds have passed.  Returns (GB/s, units, seconds)."""
     from attn_bwd_b200.generate import generate_input
@@ -215,6 +215,41 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+SOL_SHAPES = [(4, 256, 256), (8, 373, 449), (4, 1024, 2048), (64, 128, 128), (2, 256, 512),
+              (32, 691, 773), (8, 128, 128), (32, 512, 512), (4, 211, 293), (8, 256, 256),
+              (16, 128, 256), (1, 1024, 1024), (16, 256, 512), (32, 128, 128), (1, 512, 512),
+              (1, 4096, 4096)]
+
+
+def run_sol_sweep(args):
+    """The 16 SOL-ExecBench shapes (eval_modal_attn_bwd.py:18-35, sizes only), each timed
+    the way the reference evaluator does (eval_modal_attn_bwd.py:365-401): warm-up calls,
+    then L2 flush (256 MiB fill) + CUDA events around custom_kernel per rep.  Prints one
+    JSON line with per-shape µs, the geomean and the reference's score 756/geomean."""
+    import math
+    import attn_bwd_b200 as ab
+    from attn_bwd_b200.generate import generate_input_lowmem
+    torch.cuda.set_device(0)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream()
+    rows = []
+    for i, (bs, sq, skv) in enumerate(SOL_SHAPES):
+        data = generate_input_lowmem(bs, sq, skv, 1001 + i, device="cuda")
+        for _ in range(max(args.warmup, 3)):
+            ab.custom_kernel(data)
+        torch.cuda.synchronize()
+        ms = timed_loop(lambda: ab.custom_kernel(data), args.steps, flush, stream)
+        us = sum(ms) / len(ms) * 1e3
+        gbs = alg_bytes(bs * KVH, sq, skv)["total"] / (us * 1e-6) / 1e9
+        rows.append({"bs": bs, "sq": sq, "skv": skv, "us": round(us, 2), "GBps": round(gbs, 1)})
+        del data
+        torch.cuda.empty_cache()
+    assert ab.poll_error() == 0
+    geo = math.exp(sum(math.log(r["us"]) for r in rows) / len(rows))
+    print(json.dumps({"sweep": "sol-execbench-16", "geomean_us": round(geo, 2), "score": round(756.0 / geo, 3),
+                      "reference_best_snapshot_geomean_us": 379.11, "shapes": rows}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -224,10 +259,14 @@ def main():
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", choices=["sol"], default=None,
+                    help="time the 16 SOL-ExecBench shapes instead of the driver line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep == "sol":
+        return run_sol_sweep(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -16,13 +16,13 @@
 // 256), in which case pass 2 re-reads pass 1's TMEM columns.  P and the mask
 // are streamed by TMA in both passes; pass 2 re-reads them from L2.
 //
-// Roles (384 threads):
+// Roles (640 threads):
 //   warp 0  TMA producer for dO tiles and V chunks
 //   warp 1  tcgen05 MMA issuer (also owns the TMEM allocation)
-//   warp 2  TMA producer for P / mask chunks
-//   warp 3  idle
-//   warps 4..11  epilogue; warp w reads TMEM lanes 32·(w%4).. and chunk
-//                columns 32·((w-4)/4) ..+32
+//   warp 2  P / mask producer
+//   warp 3  dS store issuer (TMA tensor store of each finished chunk)
+//   warps 4..19  epilogue; warp w reads TMEM lanes 32·(w%4).. and chunk
+//                columns 16·((w-4)/4) ..+16
 //
 // Two row formats (template flag RAG):
 //   RAG = false  seq_kv % 16 == 0: P / mask chunks are TMA tensor tiles
@@ -45,7 +45,9 @@ constexpr int BM = 128;          // rows (seq_q) per unit
 constexpr int BN = 64;           // columns (seq_kv) per chunk
 constexpr int TSLOTS = 8;        // TMEM ring: 8 x 64 fp32 columns = 512
 constexpr int VST = 3;           // V chunk stages
-constexpr int kThreads = 384;
+constexpr int kEpiWarps = 16;                 // 4 per TMEM lane quadrant
+constexpr int CW = BN / (kEpiWarps / 4);      // 16 chunk columns per epilogue thread
+constexpr int kThreads = (4 + kEpiWarps) * 32;
 constexpr int kResidentMaxChunks = 4;
 constexpr int DO_BYTES = BM * kHeadDim * 2;   // 32 KB (two 64-column SW128 halves)
 constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
@@ -57,18 +59,18 @@ struct Cfg {
   static constexpr int M_PITCH = RAG ? 80 : 64;        // bytes per staged mask row
   static constexpr int P_BYTES = BM * P_PITCH;
   static constexpr int M_BYTES = BM * M_PITCH;
-  static constexpr int STG_PITCH = 80;                 // per-warp dS transpose rows (RAG)
-  static constexpr int STG_BYTES = RAG ? 8 * 32 * STG_PITCH : 0;
+  static constexpr int STG_PITCH = 48;                 // per-warp dS transpose rows (RAG): 32 B + pad
+  static constexpr int STG_BYTES = RAG ? kEpiWarps * 32 * STG_PITCH : 0;
   static constexpr int OFF_DO = 0;
   static constexpr int OFF_V = OFF_DO + 2 * DO_BYTES;
   static constexpr int OFF_P = OFF_V + VST * V_BYTES;
   static constexpr int OFF_M = OFF_P + PST * P_BYTES;
   static constexpr int OFF_STG = OFF_M + PST * M_BYTES;
   static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
-  // barriers: dO full/empty (2+2), V full/empty, PM full/empty, dS ready, T full/empty, pair (4)
+  // barriers: dO full/empty (2+2), V full/empty, PM full/empty, dS ready, T full/empty, quad (4)
   static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4;
-  static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][2][128]
-  static constexpr int OFF_MISC = OFF_RX + 2 * 2 * BM * 4;
+  static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][4][128]: per-column-group row sums
+  static constexpr int OFF_MISC = OFF_RX + 2 * 4 * BM * 4;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "dS kernel shared memory");
 };
@@ -105,50 +107,50 @@ __device__ __forceinline__ void byte_shift(const uint32_t* in, uint32_t sh, uint
   for (int j = 0; j < NOUT; ++j) out[j] = __funnelshift_r(v[j], v[j + 1], bits);
 }
 
-// Loads this thread's 32 P values (16 words of bf16 pairs) and 32 mask bytes
-// (8 words) of one chunk row from the staged chunk.
+// Loads this thread's 16 P values (8 words of bf16 pairs) and 16 mask bytes
+// (4 words) of one chunk row, column group `cg` (columns 16·cg .. +16).
 template <bool RAG>
-__device__ __forceinline__ void load_row(uint32_t p_stage, uint32_t m_stage, int row, int half, uint32_t shP,
-                                         uint32_t shM, uint32_t (&pw)[16], uint32_t (&mw)[8]) {
+__device__ __forceinline__ void load_row(uint32_t p_stage, uint32_t m_stage, int row, int cg, uint32_t shP,
+                                         uint32_t shM, uint32_t (&pw)[8], uint32_t (&mw)[4]) {
   using namespace sm100;
   if constexpr (!RAG) {
+    // TMA 128B swizzle: 16-byte chunk j of row r sits at chunk j ^ (r % 8); 64B swizzle: j ^ ((r/2) % 4)
     const uint32_t p_row = p_stage + row * 128;
-    const uint32_t m_row = m_stage + row * 64;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 t = lds128(p_row + (((half * 4 + i) ^ (row & 7)) << 4));
-      pw[4 * i] = t.x; pw[4 * i + 1] = t.y; pw[4 * i + 2] = t.z; pw[4 * i + 3] = t.w;
-    }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const uint4 t = lds128(m_row + (((half * 2 + i) ^ ((row >> 1) & 3)) << 4));
-      mw[4 * i] = t.x; mw[4 * i + 1] = t.y; mw[4 * i + 2] = t.z; mw[4 * i + 3] = t.w;
+      const uint4 t = lds128(p_row + (((cg * 2 + i) ^ (row & 7)) << 4));
+      pw[4 * i] = t.x; pw[4 * i + 1] = t.y; pw[4 * i + 2] = t.z; pw[4 * i + 3] = t.w;
     }
+    const uint4 t = lds128(m_stage + row * 64 + ((cg ^ ((row >> 1) & 3)) << 4));
+    mw[0] = t.x; mw[1] = t.y; mw[2] = t.z; mw[3] = t.w;
   } else {
-    uint32_t in[20];
-    const uint32_t p_row = p_stage + row * Cfg<true>::P_PITCH + half * 64;
+    uint32_t in[12];
+    const uint32_t p_row = p_stage + row * Cfg<true>::P_PITCH + cg * 32;
 #pragma unroll
-    for (int i = 0; i < 5; ++i) {
+    for (int i = 0; i < 3; ++i) {
       const uint4 t = lds128(p_row + i * 16);
       in[4 * i] = t.x; in[4 * i + 1] = t.y; in[4 * i + 2] = t.z; in[4 * i + 3] = t.w;
     }
-    byte_shift<16>(in, shP, pw);
-    const uint32_t m_row = m_stage + row * Cfg<true>::M_PITCH + half * 32;
+    byte_shift<8>(in, shP, pw);
+    const uint32_t m_row = m_stage + row * Cfg<true>::M_PITCH + cg * 16;
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 2; ++i) {
       const uint4 t = lds128(m_row + i * 16);
       in[4 * i] = t.x; in[4 * i + 1] = t.y; in[4 * i + 2] = t.z; in[4 * i + 3] = t.w;
     }
-    byte_shift<8>(in, shM, mw);
+    byte_shift<4>(in, shM, mw);
   }
 }
 
-// Element e (0..31) of the row: P value, and whether the score is kept.
-__device__ __forceinline__ float p_at(const uint32_t (&pw)[16], int e) {
-  return (e & 1) ? sm100::bf16hi(pw[e >> 1]) : sm100::bf16lo(pw[e >> 1]);
+// Keep-masks for 16 elements: mx[i] holds 4 bytes 0x00 / 0xFF (mask bytes are
+// bool 0/1, so ×0xFF never carries); element e's 32-bit mask is byte e%4 of
+// mx[e/4] replicated.  All-ones when the mask is not applied (p <= 0).
+__device__ __forceinline__ void expand_mask(const uint32_t (&mw)[4], int use_mask, uint32_t (&mx)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mx[i] = use_mask ? mw[i] * 0xFFu : 0xFFFFFFFFu;
 }
-__device__ __forceinline__ bool m_at(const uint32_t (&mw)[8], int e) {
-  return ((mw[e >> 2] >> ((e & 3) * 8)) & 0xFFu) != 0;
+__device__ __forceinline__ uint32_t mask_at(const uint32_t (&mx)[4], int e) {
+  return __byte_perm(mx[e >> 2], 0u, (e & 3) * 0x1111u);
 }
 
 template <bool RAG>
@@ -188,11 +190,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     for (int i = 0; i < VST; ++i) { mbar_init(&V_full[i], 1); mbar_init(&V_empty[i], 1); }
     for (int i = 0; i < PST; ++i) {
       mbar_init(&PM_full[i], 1);
-      mbar_init(&PM_empty[i], 8);
-      mbar_init(&dS_ready[i], 8);
+      mbar_init(&PM_empty[i], kEpiWarps);
+      mbar_init(&dS_ready[i], kEpiWarps);
     }
-    for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], 8); }
-    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 64);
+    for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], kEpiWarps); }
+    for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 32 * (kEpiWarps / 4));
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -355,31 +357,56 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       ++di;
     }
   mma_done:;
-  } else if (warp >= 4) {
-    // ------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int half = (warp - 4) >> 2;
+  } else if (warp == 3) {
+    // ------------------------------------------------ dS store issuer (aligned rows)
+    // Walks the same P/mask stage sequence as the epilogue; for each pass-2 chunk it
+    // waits until all epilogue warps wrote dS over the stage, stores it with one TMA
+    // tensor store, and frees the stage once the store has read shared memory.
+    if constexpr (!RAG) {
+      uint32_t pi = 0, dsr_par = 0;
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const int bhl = u / n_mb, mb = u - bhl * n_mb;
+        pi += nchunks;  // pass-1 uses of the stages
+        for (int c = 0; c < nchunks; ++c, ++pi) {
+          const int ps = pi % PST;
+          if (!warp_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306)) goto store_done;
+          dsr_par ^= 1u << ps;
+          if (lane == 0) {
+            tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
+            bulk_commit();
+            bulk_wait_read0();
+            mbar_arrive_cnt(&PM_empty[ps], kEpiWarps);
+          }
+          __syncwarp();
+        }
+      }
+    store_done:
+      if (lane == 0) bulk_wait_all0();
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 4..19)
+    const int q = warp & 3;               // TMEM lane quadrant (hardware: warp id % 4)
+    const int cg = (warp - 4) >> 2;       // column group: chunk columns 16·cg .. +16
     const int row = q * 32 + lane;
     const uint32_t t_lane = uint32_t(q * 32) << 16;
-    const bool storer = (!RAG) && (warp == 4 && lane == 0);
     const int use_mask = prm.use_mask;
     const float scale = prm.scale;
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
-    uint32_t job = 0, pi = 0, it = 0, dsr_par = 0;
+    uint32_t job = 0, pi = 0, it = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       const int s_row = mb * BM + row;
       const unsigned long long row_el = ((unsigned long long)bhl * sq + s_row) * skv;
       const uint32_t job0 = job;
-      float acc = 0.f;
-      // ---- pass 1: row sums
+      float acc0 = 0.f, acc1 = 0.f;
+      // ---- pass 1: row sums  r = Σ m·dP~·P  (the 1/(1-p) is applied once, below)
       for (int c = 0; c < nchunks; ++c) {
         const int slot = job % TSLOTS;
         if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0301)) goto epi_done;
         tc_fence_after();
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld32(tmem_base + t_lane + slot * BN + half * 32, v);
+        uint32_t v[16];
+        tmem_ld16(tmem_base + t_lane + slot * BN + cg * CW, v);
         tmem_wait_ld();
         if (!resident) {
           tc_fence_before();
@@ -390,119 +417,104 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         const int ps = pi % PST;
         if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) goto epi_done;
         const unsigned long long el = row_el + (unsigned long long)c * BN;
-        uint32_t pw[16], mw[8];
+        uint32_t pw[8], mw[4], mx[4];
         load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES),
-                      row, half, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
+                      row, cg, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
         __syncwarp();
         if (lane == 0) mbar_arrive(&PM_empty[ps]);
-        const int nvalid = RAG ? min(max(skv - (c * BN + half * 32), 0), 32) : 32;
+        expand_mask(mw, use_mask, mx);
+        const int nvalid = RAG ? min(max(skv - (c * BN + cg * CW), 0), CW) : CW;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float d = __uint_as_float(v[e]) * p_at(pw, e);
-          const bool keep = (!use_mask || m_at(mw, e)) && (!RAG || e < nvalid);
-          acc += keep ? d : 0.f;
+        for (int k = 0; k < 8; ++k) {
+          uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
+          if (RAG) {
+            m0 = (2 * k < nvalid) ? m0 : 0u;
+            m1 = (2 * k + 1 < nvalid) ? m1 : 0u;
+          }
+          acc0 = fmaf(__uint_as_float(v[2 * k]), __uint_as_float((pw[k] << 16) & m0), acc0);
+          acc1 = fmaf(__uint_as_float(v[2 * k + 1]), __uint_as_float(pw[k] & 0xFFFF0000u & m1), acc1);
         }
         ++pi;
       }
-      // ---- combine the two column halves of each row
+      // ---- combine the four column groups of each row (fixed order: deterministic)
+      float r;
       {
-        float* rxb = rx + (it & 1) * 2 * BM;
-        rxb[half * BM + row] = acc;
+        float* rxb = rx + (it & 1) * 4 * BM;
+        rxb[cg * BM + row] = acc0 + acc1;
         mbar_arrive(&pair_bar[q]);
         if (!warp_wait(&pair_bar[q], it & 1, abort_flag, err, 0x0303)) goto epi_done;
-        acc += rxb[(half ^ 1) * BM + row];
+        r = ((rxb[row] + rxb[BM + row]) + (rxb[2 * BM + row] + rxb[3 * BM + row])) * scale;
       }
-      {
-        const float r = acc * scale;
-        // ---- pass 2: dS
-        for (int c = 0; c < nchunks; ++c) {
-          int slot;
-          if (resident) {
-            slot = (job0 + c) % TSLOTS;
-          } else {
-            slot = job % TSLOTS;
-            if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0304)) goto epi_done;
-            tc_fence_after();
-            ++job;
-          }
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld32(tmem_base + t_lane + slot * BN + half * 32, v);
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&T_empty[slot]);
-          const int ps = pi % PST;
-          if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) goto epi_done;
-          const unsigned long long el = row_el + (unsigned long long)c * BN;
-          const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
-          uint32_t pw[16], mw[8];
-          load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, half, uint32_t(el * 2) & 15u,
-                        uint32_t(el) & 15u, pw, mw);
-          uint32_t o[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            float dp0 = __uint_as_float(v[2 * k]) * scale;
-            float dp1 = __uint_as_float(v[2 * k + 1]) * scale;
-            if (use_mask && !m_at(mw, 2 * k)) dp0 = 0.f;
-            if (use_mask && !m_at(mw, 2 * k + 1)) dp1 = 0.f;
-            const float p0 = p_at(pw, 2 * k), p1 = p_at(pw, 2 * k + 1);
-            o[k] = pack_bf16x2(p0 * (dp0 - r), p1 * (dp1 - r));
-          }
-          if constexpr (!RAG) {
-            // dS overwrites P in place (same swizzled positions), then one TMA store per chunk
-            const uint32_t p_row = p_stage + row * 128;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              sts128(p_row + (((half * 4 + i) ^ (row & 7)) << 4),
-                     make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dS_ready[ps]);
-            if (warp == 4) {
-              // dS_ready[ps] completes once per pass-2 use of stage ps; its parity is tracked here
-              int ok = 1;
-              if (lane == 0) {
-                ok = mbar_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306) ? 1 : 0;
-                dsr_par ^= 1u << ps;
-                if (ok) {
-                  tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
-                  bulk_commit();
-                  bulk_wait_read0();
-                  mbar_arrive_cnt(&PM_empty[ps], 8);
-                }
-              }
-              if (!__shfl_sync(0xffffffffu, ok, 0)) goto epi_done;
-            }
-          } else {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&PM_empty[ps]);
-            // transpose through the warp's buffer: row-per-thread -> column-per-lane
-            const uint32_t srow = stg + lane * C::STG_PITCH;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              sts128(srow + i * 16, make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
-            __syncwarp();
-            const int col = c * BN + half * 32 + int(lane);
-            const int rows_here = min(32, sq - (mb * BM + q * 32));
-            if (col < skv) {
-              unsigned short* dst = reinterpret_cast<unsigned short*>(prm.dS) +
-                                    ((unsigned long long)bhl * sq + mb * BM + q * 32) * skv + col;
-              for (int rr = 0; rr < rows_here; ++rr) {
-                unsigned short val;
-                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(val) : "r"(stg + rr * C::STG_PITCH + lane * 2));
-                dst[(unsigned long long)rr * skv] = val;
-              }
-            }
-            __syncwarp();
-          }
-          ++pi;
+      // ---- pass 2: dS = P · (m·dP~/(1-p) − r)
+      for (int c = 0; c < nchunks; ++c) {
+        int slot;
+        if (resident) {
+          slot = (job0 + c) % TSLOTS;
+        } else {
+          slot = job % TSLOTS;
+          if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0304)) goto epi_done;
+          tc_fence_after();
+          ++job;
         }
+        uint32_t v[16];
+        tmem_ld16(tmem_base + t_lane + slot * BN + cg * CW, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&T_empty[slot]);
+        const int ps = pi % PST;
+        if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) goto epi_done;
+        const unsigned long long el = row_el + (unsigned long long)c * BN;
+        const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
+        uint32_t pw[8], mw[4], mx[4];
+        load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, uint32_t(el * 2) & 15u,
+                      uint32_t(el) & 15u, pw, mw);
+        expand_mask(mw, use_mask, mx);
+        uint32_t o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float t0 = __uint_as_float(v[2 * k] & mask_at(mx, 2 * k));
+          const float t1 = __uint_as_float(v[2 * k + 1] & mask_at(mx, 2 * k + 1));
+          const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
+          o[k] = pack_bf16x2(p0 * fmaf(t0, scale, -r), p1 * fmaf(t1, scale, -r));
+        }
+        if constexpr (!RAG) {
+          // dS overwrites P in place (same swizzled positions); warp 3 stores the chunk
+          const uint32_t p_row = p_stage + row * 128;
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            sts128(p_row + (((cg * 2 + i) ^ (row & 7)) << 4),
+                   make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dS_ready[ps]);
+        } else {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&PM_empty[ps]);
+          // transpose through the warp's buffer: row-per-thread -> column-per-lane,
+          // then each store instruction writes 2 rows x 32 contiguous bytes
+          const uint32_t srow = stg + lane * C::STG_PITCH;
+          sts128(srow, make_uint4(o[0], o[1], o[2], o[3]));
+          sts128(srow + 16, make_uint4(o[4], o[5], o[6], o[7]));
+          __syncwarp();
+          const int col = c * BN + cg * CW + int(lane & 15);
+          const int rows_here = min(32, sq - (mb * BM + q * 32));
+          if (col < skv) {
+            unsigned short* dst = reinterpret_cast<unsigned short*>(prm.dS) +
+                                  ((unsigned long long)bhl * sq + mb * BM + q * 32) * skv + col;
+            for (int rr = int(lane >> 4); rr < rows_here; rr += 2) {
+              unsigned short val;
+              asm volatile("ld.shared.u16 %0, [%1];" : "=h"(val) : "r"(stg + rr * C::STG_PITCH + (lane & 15) * 2));
+              dst[(unsigned long long)rr * skv] = val;
+            }
+          }
+          __syncwarp();
+        }
+        ++pi;
       }
       ++it;
     }
   epi_done:
-    if (storer) bulk_wait_all0();
     __syncwarp();
   }
 
