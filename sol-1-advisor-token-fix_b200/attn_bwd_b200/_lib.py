@@ -8,7 +8,8 @@ import ctypes
 import os
 
 LIB_NAME = "libattn_bwd_b200.so"
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+# ATTN_BWD_B200_LIB may point at another build of the same library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("ATTN_BWD_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 # C-ABI error codes (enum in include/attn_bwd_b200.h)
 OK, EINVAL, EALIGN, EUNSUPPORTED, ETMAP, ECUDA, EDEVICE, EKERNEL = range(8)

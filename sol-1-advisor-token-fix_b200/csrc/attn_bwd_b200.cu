@@ -1,6 +1,7 @@
 // attn_bwd_b200.cu — C-ABI entry points: argument checks, TMA descriptors,
 // launches of the fused dS and dV kernels on the caller's stream.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -102,6 +103,19 @@ int check_shape(const Shape& s) {
   return ATTN_BWD_OK;
 }
 
+// Largest chunk count (64 seq_kv columns each) for which the dS kernel keeps a
+// unit's dP~ in TMEM between its two passes instead of recomputing it.  Up to 8
+// chunks fit; above 4 the next unit's MMAs can no longer overlap.  Tunable with
+// the environment variable ATTN_BWD_RESIDENT_MAX_CHUNKS (0..8), read once.
+int resident_max_chunks() {
+  static const int v = [] {
+    const char* e = std::getenv("ATTN_BWD_RESIDENT_MAX_CHUNKS");
+    int x = e ? std::atoi(e) : ds::kResidentMaxChunks;
+    return x < 0 ? 0 : (x > ds::TSLOTS ? ds::TSLOTS : x);
+  }();
+  return v;
+}
+
 // seq_kv rows of P / mask / dS must be 16-byte multiples for the TMA path.
 inline bool tma_rows_ok(int skv) { return (skv % 16) == 0; }
 
@@ -144,7 +158,7 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.n_mb = (s.sq + ds::BM - 1) / ds::BM;
   prm.n_units = nbh * prm.n_mb;
   prm.nchunks = (s.skv + ds::BN - 1) / ds::BN;
-  prm.resident = prm.nchunks <= ds::kResidentMaxChunks ? 1 : 0;
+  prm.resident = prm.nchunks <= resident_max_chunks() ? 1 : 0;
   prm.bh_base = s.u0 * kGroups;
   prm.use_mask = p > 0.f ? 1 : 0;
   prm.scale = p > 0.f ? 1.0f / (1.0f - p) : 1.0f;
@@ -317,5 +331,16 @@ const char* attn_bwd_b200_strerror(int code) {
 }
 
 int attn_bwd_b200_version(void) { return 100; }
+
+#ifdef ATTN_BWD_WAIT_STATS
+// Diagnostics builds only (not part of the ABI): copies and clears the per-site wait cycles.
+int attn_bwd_b200_wait_stats(unsigned long long* out) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return ATTN_BWD_ECUDA;
+  if (cudaMemcpyFromSymbol(out, sm100::g_wait_cycles, sizeof(unsigned long long) * 128) != cudaSuccess)
+    return ATTN_BWD_ECUDA;
+  static const unsigned long long zero[128] = {};
+  return cudaMemcpyToSymbol(sm100::g_wait_cycles, zero, sizeof(zero)) == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
+}
+#endif
 
 }  // extern "C"

@@ -44,7 +44,17 @@ namespace ds {
 constexpr int BM = 128;          // rows (seq_q) per unit
 constexpr int BN = 64;           // columns (seq_kv) per chunk
 constexpr int TSLOTS = 8;        // TMEM ring: 8 x 64 fp32 columns = 512
-constexpr int VST = 3;           // V chunk stages
+#ifndef ATTN_BWD_DS_VST
+#define ATTN_BWD_DS_VST 3
+#endif
+#ifndef ATTN_BWD_DS_PST
+#define ATTN_BWD_DS_PST 4
+#endif
+#ifndef ATTN_BWD_DS_DOBUF
+#define ATTN_BWD_DS_DOBUF 2
+#endif
+constexpr int VST = ATTN_BWD_DS_VST;   // V chunk stages
+constexpr int DOBUF = ATTN_BWD_DS_DOBUF;  // dO tile buffers
 constexpr int kEpiWarps = 16;                 // 4 per TMEM lane quadrant
 constexpr int CW = BN / (kEpiWarps / 4);      // 16 chunk columns per epilogue thread
 constexpr int kThreads = (4 + kEpiWarps) * 32;
@@ -54,7 +64,7 @@ constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 
 template <bool RAG>
 struct Cfg {
-  static constexpr int PST = RAG ? 3 : 4;              // P/mask chunk stages
+  static constexpr int PST = RAG ? 3 : ATTN_BWD_DS_PST;  // P/mask chunk stages
   static constexpr int P_PITCH = RAG ? 144 : 128;      // bytes per staged P row
   static constexpr int M_PITCH = RAG ? 80 : 64;        // bytes per staged mask row
   static constexpr int P_BYTES = BM * P_PITCH;
@@ -62,7 +72,7 @@ struct Cfg {
   static constexpr int STG_PITCH = 48;                 // per-warp dS transpose rows (RAG): 32 B + pad
   static constexpr int STG_BYTES = RAG ? kEpiWarps * 32 * STG_PITCH : 0;
   static constexpr int OFF_DO = 0;
-  static constexpr int OFF_V = OFF_DO + 2 * DO_BYTES;
+  static constexpr int OFF_V = OFF_DO + DOBUF * DO_BYTES;
   static constexpr int OFF_P = OFF_V + VST * V_BYTES;
   static constexpr int OFF_M = OFF_P + PST * P_BYTES;
   static constexpr int OFF_STG = OFF_M + PST * M_BYTES;
@@ -186,7 +196,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   const uint32_t lane = lane_id();
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) { mbar_init(&dO_full[i], 1); mbar_init(&dO_empty[i], 1); }
+    for (int i = 0; i < DOBUF; ++i) { mbar_init(&dO_full[i], 1); mbar_init(&dO_empty[i], 1); }
     for (int i = 0; i < VST; ++i) { mbar_init(&V_full[i], 1); mbar_init(&V_empty[i], 1); }
     for (int i = 0; i < PST; ++i) {
       mbar_init(&PM_full[i], 1);
@@ -225,8 +235,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       const int bh = prm.bh_base + bhl;
       const int b = bh / kHeads, h = bh - b * kHeads;
       const int zv = b * kKvHeads + h / kGroups;
-      const int db = di & 1;
-      if (!warp_wait(&dO_empty[db], ((di >> 1) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
+      const int db = di % DOBUF;
+      if (!warp_wait(&dO_empty[db], ((di / DOBUF) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
       if (lane == 0) {
         mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
         tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
@@ -250,9 +260,9 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   producer_done:
     // drain: the last issue of every stage must have landed before exit
     if (lane == 0) {
-      for (uint32_t k = 0; k < 2 && k < di; ++k) {
+      for (uint32_t k = 0; k < uint32_t(DOBUF) && k < di; ++k) {
         const uint32_t i = di - 1 - k;
-        mbar_drain(&dO_full[i & 1], (i >> 1) & 1, err, 0x0111);
+        mbar_drain(&dO_full[i % DOBUF], (i / DOBUF) & 1, err, 0x0111);
       }
       for (uint32_t k = 0; k < uint32_t(VST) && k < vi; ++k) {
         const uint32_t i = vi - 1 - k;
@@ -323,8 +333,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
     uint32_t job = 0, vi = 0, di = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const int db = di & 1;
-      if (!warp_wait(&dO_full[db], (di >> 1) & 1, abort_flag, err, 0x0201)) goto mma_done;
+      const int db = di % DOBUF;
+      if (!warp_wait(&dO_full[db], (di / DOBUF) & 1, abort_flag, err, 0x0201)) goto mma_done;
       const uint32_t a_base = smem_u32(smem + C::OFF_DO + db * DO_BYTES);
       for (int pass = 0; pass < npass_mma; ++pass) {
         for (int c = 0; c < nchunks; ++c) {

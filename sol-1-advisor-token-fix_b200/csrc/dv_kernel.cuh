@@ -82,6 +82,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
   using namespace sm100;
   using C = Cfg<RAG>;
   constexpr int ST = C::ST, RST = C::RST;
+  constexpr int RSTD = RST > 0 ? RST : 1;  // keeps the (unused) ragged arithmetic defined when RST == 0
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -142,8 +143,8 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
           }
           ++si;
           if constexpr (RAG) {
-            const int rs = ri % RST;
-            if (!warp_wait(&raw_empty[rs], ((ri / RST) & 1) ^ 1, abort_flag, err, 0x1102)) goto prod_done;
+            const int rs = ri % RSTD;
+            if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1102)) goto prod_done;
             unsigned long long src[2];
             uint32_t sz[2], total = 0;
 #pragma unroll
@@ -182,7 +183,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
       }
       for (uint32_t k = 0; k < uint32_t(RST) && k < ri; ++k) {
         const uint32_t i = ri - 1 - k;
-        mbar_drain(&raw_full[i % RST], (i / RST) & 1, err, 0x1112);
+        mbar_drain(&raw_full[i % RSTD], (i / RSTD) & 1, err, 0x1112);
       }
     }
     __syncwarp();
@@ -272,8 +273,8 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
       for (int g = 0; g < kGroups; ++g) {
         const int bhl = ul * kGroups + g;
         for (int kc = 0; kc < n_kc; ++kc, ++si) {
-          const int s = si % ST, rs = si % RST;
-          if (!warp_wait(&raw_full[rs], (si / RST) & 1, abort_flag, err, 0x1401)) goto realign_done;
+          const int s = si % ST, rs = si % RSTD;
+          if (!warp_wait(&raw_full[rs], (si / RSTD) & 1, abort_flag, err, 0x1401)) goto realign_done;
           if (!warp_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1402)) goto realign_done;
           const int srow = kc * BK + r;
           uint32_t w[32];

@@ -96,10 +96,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Warp-uniform bounded wait: all 32 lanes poll (each gets the barrier's acquire
 // ordering) and the outcome is agreed with a vote, so on a timeout the whole
 // warp leaves together and no lane is left behind in a __syncwarp.
+#ifdef ATTN_BWD_WAIT_STATS
+// Diagnostics builds only: cycles each warp spent in each wait site (index from the site code).
+__device__ unsigned long long g_wait_cycles[128];
+#endif
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
                                           int code) {
+#ifdef ATTN_BWD_WAIT_STATS
+  const long long t0 = clock64();
+#endif
   const bool ok = mbar_wait(bar, parity, abort, err, code);
-  return __all_sync(0xffffffffu, ok);
+  const bool all = __all_sync(0xffffffffu, ok);
+#ifdef ATTN_BWD_WAIT_STATS
+  if ((threadIdx.x & 31) == 0)
+    atomicAdd(&g_wait_cycles[(((code >> 8) & 0xF) * 8 + (code & 7)) & 127], (unsigned long long)(clock64() - t0));
+#endif
+  return all;
 }
 
 // Drain wait used on the way out of a producer: waits (bounded, ignoring the
