@@ -43,10 +43,14 @@ int device_state(DeviceState** out) {
     } else if (major != 10) {
       st.rc = ATTN_BWD_EDEVICE;
     } else if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-               cudaFuncSetAttribute(ds::ds_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ds::Cfg<false>::SMEM_BYTES) != cudaSuccess ||
-               cudaFuncSetAttribute(ds::ds_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ds::Cfg<true>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(ds::ds_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ds::Cfg<false, false>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(ds::ds_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ds::Cfg<false, true>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(ds::ds_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ds::Cfg<true, false>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(ds::ds_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ds::Cfg<true, true>::SMEM_BYTES) != cudaSuccess ||
                cudaFuncSetAttribute(dv::dv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     dv::Cfg<false>::SMEM_BYTES) != cudaSuccess ||
                cudaFuncSetAttribute(dv::dv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -104,9 +108,10 @@ int check_shape(const Shape& s) {
 }
 
 // Largest chunk count (64 seq_kv columns each) for which the dS kernel keeps a
-// unit's dP~ in TMEM between its two passes instead of recomputing it.  Up to 8
-// chunks fit; above 4 the next unit's MMAs can no longer overlap.  Tunable with
-// the environment variable ATTN_BWD_RESIDENT_MAX_CHUNKS (0..8), read once.
+// unit's dP~ in TMEM between its two passes instead of recomputing it: all 8
+// chunks of the TMEM ring (seq_kv <= 512).  Measured on B200: resident beats
+// recompute at 6 and 8 chunks even though the next unit's MMAs then wait for
+// the ring.  Tunable with ATTN_BWD_RESIDENT_MAX_CHUNKS (0..8), read once.
 int resident_max_chunks() {
   static const int v = [] {
     const char* e = std::getenv("ATTN_BWD_RESIDENT_MAX_CHUNKS");
@@ -170,10 +175,15 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.p_end16 = (E * 2 + 15) & ~15ull;
   prm.m_end16 = (E + 15) & ~15ull;
   const int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
-  if (rag)
-    ds::ds_kernel<true><<<grid, ds::kThreads, ds::Cfg<true>::SMEM_BYTES, stream>>>(tm_dO, tm_V, tm_P, tm_M, tm_dS, prm);
-  else
-    ds::ds_kernel<false><<<grid, ds::kThreads, ds::Cfg<false>::SMEM_BYTES, stream>>>(tm_dO, tm_V, tm_P, tm_M, tm_dS, prm);
+#define ATTN_BWD_LAUNCH_DS(R, S)                                                                         \
+  ds::ds_kernel<R, S><<<grid, ds::kThreads, ds::Cfg<R, S>::SMEM_BYTES, stream>>>(tm_dO, tm_V, tm_P, tm_M, tm_dS, \
+                                                                                 prm)
+  if (rag) {
+    if (prm.resident) ATTN_BWD_LAUNCH_DS(true, true); else ATTN_BWD_LAUNCH_DS(true, false);
+  } else {
+    if (prm.resident) ATTN_BWD_LAUNCH_DS(false, true); else ATTN_BWD_LAUNCH_DS(false, false);
+  }
+#undef ATTN_BWD_LAUNCH_DS
   return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 

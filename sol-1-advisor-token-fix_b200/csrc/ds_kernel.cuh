@@ -44,29 +44,25 @@ namespace ds {
 constexpr int BM = 128;          // rows (seq_q) per unit
 constexpr int BN = 64;           // columns (seq_kv) per chunk
 constexpr int TSLOTS = 8;        // TMEM ring: 8 x 64 fp32 columns = 512
-#ifndef ATTN_BWD_DS_VST
-#define ATTN_BWD_DS_VST 3
-#endif
-#ifndef ATTN_BWD_DS_PST
-#define ATTN_BWD_DS_PST 4
-#endif
-#ifndef ATTN_BWD_DS_DOBUF
-#define ATTN_BWD_DS_DOBUF 2
-#endif
-constexpr int VST = ATTN_BWD_DS_VST;   // V chunk stages
-constexpr int DOBUF = ATTN_BWD_DS_DOBUF;  // dO tile buffers
+constexpr int RAG_P_PITCH = 144;   // ragged rows: 128 B of P row + 16 B of misalignment slack
+constexpr int RAG_M_PITCH = 80;    // ragged rows: 64 B of mask row + 16 B of slack
 constexpr int kEpiWarps = 16;                 // 4 per TMEM lane quadrant
 constexpr int CW = BN / (kEpiWarps / 4);      // 16 chunk columns per epilogue thread
 constexpr int kThreads = (4 + kEpiWarps) * 32;
-constexpr int kResidentMaxChunks = 4;
+constexpr int kResidentMaxChunks = TSLOTS;
 constexpr int DO_BYTES = BM * kHeadDim * 2;   // 32 KB (two 64-column SW128 halves)
 constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 
-template <bool RAG>
+// Shared-memory plan per mode.  RES (dP~ resident in TMEM between the passes):
+// the MMAs of a unit end with pass 1, so one dO buffer suffices and the freed
+// space buys P/mask stages (bytes in flight are what keep HBM busy).
+template <bool RAG, bool RES>
 struct Cfg {
-  static constexpr int PST = RAG ? 3 : ATTN_BWD_DS_PST;  // P/mask chunk stages
-  static constexpr int P_PITCH = RAG ? 144 : 128;      // bytes per staged P row
-  static constexpr int M_PITCH = RAG ? 80 : 64;        // bytes per staged mask row
+  static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
+  static constexpr int VST = 2;                        // V chunk stages
+  static constexpr int PST = RAG ? (RES ? 4 : 3) : (RES ? 6 : 5);  // P/mask chunk stages
+  static constexpr int P_PITCH = RAG ? RAG_P_PITCH : 128;  // bytes per staged P row
+  static constexpr int M_PITCH = RAG ? RAG_M_PITCH : 64;   // bytes per staged mask row
   static constexpr int P_BYTES = BM * P_PITCH;
   static constexpr int M_BYTES = BM * M_PITCH;
   static constexpr int STG_PITCH = 48;                 // per-warp dS transpose rows (RAG): 32 B + pad
@@ -79,6 +75,7 @@ struct Cfg {
   static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   // barriers: dO full/empty (2+2), V full/empty, PM full/empty, dS ready, T full/empty, quad (4)
   static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4;
+  static_assert(DOBUF <= 2, "two dO barrier slots");
   static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][4][128]: per-column-group row sums
   static constexpr int OFF_MISC = OFF_RX + 2 * 4 * BM * 4;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
@@ -135,14 +132,14 @@ __device__ __forceinline__ void load_row(uint32_t p_stage, uint32_t m_stage, int
     mw[0] = t.x; mw[1] = t.y; mw[2] = t.z; mw[3] = t.w;
   } else {
     uint32_t in[12];
-    const uint32_t p_row = p_stage + row * Cfg<true>::P_PITCH + cg * 32;
+    const uint32_t p_row = p_stage + row * RAG_P_PITCH + cg * 32;
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
       const uint4 t = lds128(p_row + i * 16);
       in[4 * i] = t.x; in[4 * i + 1] = t.y; in[4 * i + 2] = t.z; in[4 * i + 3] = t.w;
     }
     byte_shift<8>(in, shP, pw);
-    const uint32_t m_row = m_stage + row * Cfg<true>::M_PITCH + cg * 16;
+    const uint32_t m_row = m_stage + row * RAG_M_PITCH + cg * 16;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const uint4 t = lds128(m_row + i * 16);
@@ -163,7 +160,7 @@ __device__ __forceinline__ uint32_t mask_at(const uint32_t (&mx)[4], int e) {
   return __byte_perm(mx[e >> 2], 0u, (e & 3) * 0x1111u);
 }
 
-template <bool RAG>
+template <bool RAG, bool RES>
 __global__ void __launch_bounds__(kThreads, 1)
 ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64,1,128,1) SW128
           const __grid_constant__ CUtensorMap tm_V,    // (d, skv, b·8)  box (64,64,1)    SW128
@@ -172,8 +169,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const __grid_constant__ CUtensorMap tm_dS,   // (skv, sq, bh)  box (64,128,1)   SW128 (aligned only)
           const Params prm) {
   using namespace sm100;
-  using C = Cfg<RAG>;
-  constexpr int PST = C::PST;
+  using C = Cfg<RAG, RES>;
+  constexpr int PST = C::PST, VST = C::VST, DOBUF = C::DOBUF;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -199,7 +196,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     for (int i = 0; i < DOBUF; ++i) { mbar_init(&dO_full[i], 1); mbar_init(&dO_empty[i], 1); }
     for (int i = 0; i < VST; ++i) { mbar_init(&V_full[i], 1); mbar_init(&V_empty[i], 1); }
     for (int i = 0; i < PST; ++i) {
-      mbar_init(&PM_full[i], 1);
+      mbar_init(&PM_full[i], RAG ? 32 : 1);   // RAG: one cp.async completion arrive per producer lane
       mbar_init(&PM_empty[i], kEpiWarps);
       mbar_init(&dS_ready[i], kEpiWarps);
     }
@@ -223,8 +220,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
 
   const int n_units = prm.n_units, n_mb = prm.n_mb, nchunks = prm.nchunks;
   const int sq = prm.sq, skv = prm.skv;
-  const bool resident = prm.resident != 0;
-  const int npass_mma = resident ? 1 : 2;
+  constexpr bool resident = RES;
+  constexpr int npass_mma = RES ? 1 : 2;
   int* err = prm.err;
 
   if (warp == 0) {
@@ -286,41 +283,37 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
               tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
             }
           } else {
-            unsigned long long srcp[4], srcm[4];
-            uint32_t szp[4], szm[4], total = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int s = mb * BM + int(lane) + 32 * k;
-              szp[k] = szm[k] = 0;
-              srcp[k] = srcm[k] = 0;
-              if (s < sq) {
-                const unsigned long long el = ((unsigned long long)bhl * sq + s) * skv + (unsigned long long)c * BN;
-                srcp[k] = (el * 2) & ~15ull;
-                srcm[k] = el & ~15ull;
-                const unsigned long long rp = prm.p_end16 - srcp[k], rm = prm.m_end16 - srcm[k];
-                szp[k] = rp < (unsigned long long)C::P_PITCH ? uint32_t(rp) : uint32_t(C::P_PITCH);
-                szm[k] = rm < (unsigned long long)C::M_PITCH ? uint32_t(rm) : uint32_t(C::M_PITCH);
-                total += szp[k] + szm[k];
+            // 16-byte cp.async of the aligned words covering each row segment (9 for P,
+            // 5 for the mask), spread over the 32 lanes; words past the tensor's end
+            // (rounded up to 16 bytes) are skipped, their columns are masked later.
+            const uint32_t pdst = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
+            const uint32_t mdst = smem_u32(smem + C::OFF_M + ps * C::M_BYTES);
+            for (int i = int(lane); i < BM * 9; i += 32) {
+              const int r = i / 9, w = i - r * 9;
+              const int srow = mb * BM + r;
+              if (srow < sq) {
+                const unsigned long long el = ((unsigned long long)bhl * sq + srow) * skv + (unsigned long long)c * BN;
+                const unsigned long long src = ((el * 2) & ~15ull) + 16ull * w;
+                if (src < prm.p_end16) cp_async16(pdst + r * C::P_PITCH + w * 16, prm.P + src);
               }
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-            if (lane == 0) mbar_arrive_expect_tx(&PM_full[ps], total);
-            __syncwarp();
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int r = int(lane) + 32 * k;
-              if (szp[k]) {
-                bulk_load(smem + C::OFF_P + ps * C::P_BYTES + r * C::P_PITCH, prm.P + srcp[k], szp[k], &PM_full[ps]);
-                bulk_load(smem + C::OFF_M + ps * C::M_BYTES + r * C::M_PITCH, prm.M + srcm[k], szm[k], &PM_full[ps]);
+            for (int i = int(lane); i < BM * 5; i += 32) {
+              const int r = i / 5, w = i - r * 5;
+              const int srow = mb * BM + r;
+              if (srow < sq) {
+                const unsigned long long el = ((unsigned long long)bhl * sq + srow) * skv + (unsigned long long)c * BN;
+                const unsigned long long src = (el & ~15ull) + 16ull * w;
+                if (src < prm.m_end16) cp_async16(mdst + r * C::M_PITCH + w * 16, prm.M + src);
               }
             }
+            cp_async_arrive_noinc(&PM_full[ps]);
           }
           ++pi;
         }
       }
     }
   pm_done:
+    if (RAG) cp_async_wait_all();
     if (lane == 0) {
       for (uint32_t k = 0; k < uint32_t(PST) && k < pi; ++k) {
         const uint32_t i = pi - 1 - k;

@@ -99,7 +99,8 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
   const uint32_t warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 4); }
-    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 4); }
+    // raw_full: one cp.async completion arrive per producer lane
+    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 32); mbar_init(&raw_empty[i], 4); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     fence_barrier_init();
@@ -145,43 +146,34 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
           if constexpr (RAG) {
             const int rs = ri % RSTD;
             if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1102)) goto prod_done;
-            unsigned long long src[2];
-            uint32_t sz[2], total = 0;
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              const int srow = kc * BK + int(lane) + 32 * k;
-              sz[k] = 0;
-              src[k] = 0;
+            // 16-byte cp.async of the 17 aligned words covering each 128-column row
+            // segment, spread over the 32 lanes; words past the tensor's end (rounded up
+            // to 16 bytes) are skipped, the re-align warps zero those columns.
+            const uint32_t rdst = smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES);
+            for (int i = int(lane); i < BK * 17; i += 32) {
+              const int r = i / 17, w = i - r * 17;
+              const int srow = kc * BK + r;
               if (srow < prm.sq) {
                 const unsigned long long el =
                     ((unsigned long long)bhl * prm.sq + srow) * prm.skv + (unsigned long long)jt * BM;
-                src[k] = (el * 2) & ~15ull;
-                const unsigned long long rem = prm.pd_end16 - src[k];
-                sz[k] = rem < (unsigned long long)C::RAW_PITCH ? uint32_t(rem) : uint32_t(C::RAW_PITCH);
-                total += sz[k];
+                const unsigned long long src = ((el * 2) & ~15ull) + 16ull * w;
+                if (src < prm.pd_end16) cp_async16(rdst + r * C::RAW_PITCH + w * 16, prm.Pd + src);
               }
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-            if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], total);
-            __syncwarp();
-#pragma unroll
-            for (int k = 0; k < 2; ++k)
-              if (sz[k])
-                bulk_load(smem + C::OFF_RAW + rs * C::RAW_BYTES + (int(lane) + 32 * k) * C::RAW_PITCH, prm.Pd + src[k],
-                          sz[k], &raw_full[rs]);
+            cp_async_arrive_noinc(&raw_full[rs]);
             ++ri;
           }
         }
       }
     }
   prod_done:
+    if (RAG) cp_async_wait_all();
     if (lane == 0) {
       for (uint32_t k = 0; k < uint32_t(ST) && k < si; ++k) {
         const uint32_t i = si - 1 - k;
         mbar_drain(&full[i % ST], (i / ST) & 1, err, 0x1111);
       }
-      for (uint32_t k = 0; k < uint32_t(RST) && k < ri; ++k) {
+      for (uint32_t k = 0; RST > 0 && k < uint32_t(RSTD) && k < ri; ++k) {
         const uint32_t i = ri - 1 - k;
         mbar_drain(&raw_full[i % RSTD], (i / RSTD) & 1, err, 0x1112);
       }
