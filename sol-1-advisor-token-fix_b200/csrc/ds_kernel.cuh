@@ -59,8 +59,8 @@ constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 template <bool RAG, bool RES>
 struct Cfg {
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
-  static constexpr int VST = 2;                        // V chunk stages
-  static constexpr int PST = RAG ? (RES ? 4 : 3) : (RES ? 6 : 5);  // P/mask chunk stages
+  static constexpr int VST = RES ? 2 : 3;              // V chunk stages (non-resident: V read twice)
+  static constexpr int PST = RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);  // P/mask chunk stages
   static constexpr int P_PITCH = RAG ? RAG_P_PITCH : 128;  // bytes per staged P row
   static constexpr int M_PITCH = RAG ? RAG_M_PITCH : 64;   // bytes per staged mask row
   static constexpr int P_BYTES = BM * P_PITCH;
@@ -196,7 +196,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     for (int i = 0; i < DOBUF; ++i) { mbar_init(&dO_full[i], 1); mbar_init(&dO_empty[i], 1); }
     for (int i = 0; i < VST; ++i) { mbar_init(&V_full[i], 1); mbar_init(&V_empty[i], 1); }
     for (int i = 0; i < PST; ++i) {
-      mbar_init(&PM_full[i], RAG ? 32 : 1);   // RAG: one cp.async completion arrive per producer lane
+      mbar_init(&PM_full[i], RAG ? 64 : 1);   // RAG: one cp.async completion arrive per producer lane (2 warps)
       mbar_init(&PM_empty[i], kEpiWarps);
       mbar_init(&dS_ready[i], kEpiWarps);
     }
@@ -267,8 +267,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       }
     }
     __syncwarp();
-  } else if (warp == 2) {
-    // ------------------------------------------------ P / mask producer
+  } else if (warp == 2 || (RAG && warp == 3)) {
+    // ------------------------------------------------ P / mask producer (RAG: warps 2 and 3)
     uint32_t pi = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
@@ -283,28 +283,25 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
               tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
             }
           } else {
-            // 16-byte cp.async of the aligned words covering each row segment (9 for P,
-            // 5 for the mask), spread over the 32 lanes; words past the tensor's end
-            // (rounded up to 16 bytes) are skipped, their columns are masked later.
+            // 16-byte cp.async of the aligned words covering each row segment: 9 for P,
+            // 5 for the mask.  Warp 2 takes rows 0..63, warp 3 rows 64..127; lane =
+            // (row offset lane/8, word lane%8) so 4 rows go per step and the row start
+            // advances by an add.  Words past the tensor's end (rounded up to 16 bytes)
+            // are skipped; their columns are masked by the consumers.
             const uint32_t pdst = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
             const uint32_t mdst = smem_u32(smem + C::OFF_M + ps * C::M_BYTES);
-            for (int i = int(lane); i < BM * 9; i += 32) {
-              const int r = i / 9, w = i - r * 9;
-              const int srow = mb * BM + r;
-              if (srow < sq) {
-                const unsigned long long el = ((unsigned long long)bhl * sq + srow) * skv + (unsigned long long)c * BN;
-                const unsigned long long src = ((el * 2) & ~15ull) + 16ull * w;
-                if (src < prm.p_end16) cp_async16(pdst + r * C::P_PITCH + w * 16, prm.P + src);
-              }
-            }
-            for (int i = int(lane); i < BM * 5; i += 32) {
-              const int r = i / 5, w = i - r * 5;
-              const int srow = mb * BM + r;
-              if (srow < sq) {
-                const unsigned long long el = ((unsigned long long)bhl * sq + srow) * skv + (unsigned long long)c * BN;
-                const unsigned long long src = (el & ~15ull) + 16ull * w;
-                if (src < prm.m_end16) cp_async16(mdst + r * C::M_PITCH + w * 16, prm.M + src);
-              }
+            const int w = int(lane & 7);
+            const int r0 = (warp == 2 ? 0 : BM / 2) + int(lane >> 3);
+            const int rows = min(BM / 2, sq - mb * BM - (warp == 2 ? 0 : BM / 2));
+            unsigned long long el = ((unsigned long long)bhl * sq + mb * BM + r0) * skv + (unsigned long long)c * BN;
+            const unsigned long long step = 4ull * skv;
+            for (int k = 0; 4 * k + int(lane >> 3) < rows; ++k, el += step) {
+              const int r = r0 + 4 * k;
+              const unsigned long long sp = ((el * 2) & ~15ull) + 16ull * w;
+              const unsigned long long sm_ = (el & ~15ull) + 16ull * w;
+              if (sp < prm.p_end16) cp_async16(pdst + r * C::P_PITCH + w * 16, prm.P + sp);
+              if (w == 0 && sp + 128 < prm.p_end16) cp_async16(pdst + r * C::P_PITCH + 128, prm.P + sp + 128);
+              if (w < 5 && sm_ < prm.m_end16) cp_async16(mdst + r * C::M_PITCH + w * 16, prm.M + sm_);
             }
             cp_async_arrive_noinc(&PM_full[ps]);
           }
@@ -314,7 +311,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     }
   pm_done:
     if (RAG) cp_async_wait_all();
-    if (lane == 0) {
+    if (lane == 0 && warp == 2) {
       for (uint32_t k = 0; k < uint32_t(PST) && k < pi; ++k) {
         const uint32_t i = pi - 1 - k;
         mbar_drain(&PM_full[i % PST], (i / PST) & 1, err, 0x0113);

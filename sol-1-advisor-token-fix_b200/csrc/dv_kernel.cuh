@@ -36,10 +36,10 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
 template <bool RAG>
 struct Cfg {
-  static constexpr int kThreads = RAG ? 320 : 192;
+  static constexpr int kThreads = RAG ? 352 : 192;   // RAG: + 4 re-align warps + 1 extra raw-row producer
   static constexpr int ST = RAG ? 4 : 6;               // operand stages
   static constexpr int RST = RAG ? 4 : 0;              // raw P_drop row stages
-  static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack
+  static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack (raw_rows_async)
   static constexpr int RAW_BYTES = BK * RAW_PITCH;
   static constexpr int OFF_RAW = ST * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_RAW + RST * RAW_BYTES;
@@ -73,6 +73,27 @@ __device__ __forceinline__ void byte_shift(const uint32_t* in, uint32_t sh, uint
   for (int j = 0; j < NOUT; ++j) out[j] = __funnelshift_r(v[j], v[j + 1], bits);
 }
 
+// Ragged P_drop rows: 16-byte cp.async of the 17 aligned words covering the
+// 128-column segment of rows [r_base, r_base+32) of a K chunk.  Lane = (row
+// offset lane/16, word lane%16; lane%16 == 0 also takes word 16), two rows per
+// step, the row start advanced by an add.  Words past the tensor's end (rounded
+// up to 16 bytes) are skipped; the re-align warps zero those columns.
+__device__ __forceinline__ void raw_rows_async(uint32_t rdst, const Params& prm, int bhl, int kc, int jt, int r_base,
+                                               uint32_t lane) {
+  constexpr int PITCH = 272;
+  const int w = int(lane & 15);
+  const int r0 = r_base + int(lane >> 4);
+  const int rows = min(32, prm.sq - kc * BK - r_base);
+  unsigned long long el = ((unsigned long long)bhl * prm.sq + kc * BK + r0) * prm.skv + (unsigned long long)jt * BM;
+  const unsigned long long step = 2ull * prm.skv;
+  for (int k = 0; 2 * k + int(lane >> 4) < rows; ++k, el += step) {
+    const int r = r0 + 2 * k;
+    const unsigned long long src = ((el * 2) & ~15ull) + 16ull * w;
+    if (src < prm.pd_end16) sm100::cp_async16(rdst + r * PITCH + w * 16, prm.Pd + src);
+    if (w == 0 && src + 256 < prm.pd_end16) sm100::cp_async16(rdst + r * PITCH + 256, prm.Pd + src + 256);
+  }
+}
+
 template <bool RAG>
 __global__ void __launch_bounds__(Cfg<RAG>::kThreads, 1)
 dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  box (64,64,1) SW128
@@ -99,8 +120,8 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
   const uint32_t warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 4); }
-    // raw_full: one cp.async completion arrive per producer lane
-    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 32); mbar_init(&raw_empty[i], 4); }
+    // raw_full: one cp.async completion arrive per lane of the two raw-row producer warps
+    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 64); mbar_init(&raw_empty[i], 4); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     fence_barrier_init();
@@ -146,20 +167,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
           if constexpr (RAG) {
             const int rs = ri % RSTD;
             if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1102)) goto prod_done;
-            // 16-byte cp.async of the 17 aligned words covering each 128-column row
-            // segment, spread over the 32 lanes; words past the tensor's end (rounded up
-            // to 16 bytes) are skipped, the re-align warps zero those columns.
-            const uint32_t rdst = smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES);
-            for (int i = int(lane); i < BK * 17; i += 32) {
-              const int r = i / 17, w = i - r * 17;
-              const int srow = kc * BK + r;
-              if (srow < prm.sq) {
-                const unsigned long long el =
-                    ((unsigned long long)bhl * prm.sq + srow) * prm.skv + (unsigned long long)jt * BM;
-                const unsigned long long src = ((el * 2) & ~15ull) + 16ull * w;
-                if (src < prm.pd_end16) cp_async16(rdst + r * C::RAW_PITCH + w * 16, prm.Pd + src);
-              }
-            }
+            raw_rows_async(smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES), prm, bhl, kc, jt, 0, lane);
             cp_async_arrive_noinc(&raw_full[rs]);
             ++ri;
           }
@@ -252,6 +260,25 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
     }
   }
 
+  else if (RAG && warp == 10) {
+    // second raw-row producer: rows 32..63 of every K chunk (warp 0 does rows 0..31)
+    uint32_t ri = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int ul = u / n_jt, jt = u - ul * n_jt;
+      for (int g = 0; g < kGroups; ++g) {
+        const int bhl = ul * kGroups + g;
+        for (int kc = 0; kc < n_kc; ++kc, ++ri) {
+          const int rs = ri % RSTD;
+          if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1103)) goto raw2_done;
+          raw_rows_async(smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES), prm, bhl, kc, jt, 32, lane);
+          cp_async_arrive_noinc(&raw_full[rs]);
+        }
+      }
+    }
+  raw2_done:
+    cp_async_wait_all();
+    __syncwarp();
+  }
   else if (RAG) {
     // re-align warps 6..9: thread t handles row r = t % 64 of the chunk and the
     // 64-column MN block jb = t / 64
