@@ -163,7 +163,16 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.n_mb = (s.sq + ds::BM - 1) / ds::BM;
   prm.n_units = nbh * prm.n_mb;
   prm.nchunks = (s.skv + ds::BN - 1) / ds::BN;
-  prm.resident = prm.nchunks <= resident_max_chunks() ? 1 : 0;
+  // Rows longer than the TMEM ring (8 chunks = 512 columns) are split over a
+  // cluster of cs <= 8 CTAs so every CTA's column slice stays resident; only rows
+  // beyond 8 x 512 columns fall back to recomputing dP~ in pass 2.
+  prm.cs = 1;
+  prm.cpc = prm.nchunks;
+  if (prm.nchunks > ds::TSLOTS && prm.nchunks <= 8 * ds::TSLOTS && resident_max_chunks() == ds::TSLOTS) {
+    prm.cs = (prm.nchunks + ds::TSLOTS - 1) / ds::TSLOTS;
+    prm.cpc = (prm.nchunks + prm.cs - 1) / prm.cs;
+  }
+  prm.resident = prm.cpc <= resident_max_chunks() ? 1 : 0;
   prm.bh_base = s.u0 * kGroups;
   prm.use_mask = p > 0.f ? 1 : 0;
   prm.scale = p > 0.f ? 1.0f / (1.0f - p) : 1.0f;
@@ -174,16 +183,39 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   const unsigned long long E = (unsigned long long)nbh * s.sq * s.skv;
   prm.p_end16 = (E * 2 + 15) & ~15ull;
   prm.m_end16 = (E + 15) & ~15ull;
-  const int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
-#define ATTN_BWD_LAUNCH_DS(R, S)                                                                         \
-  ds::ds_kernel<R, S><<<grid, ds::kThreads, ds::Cfg<R, S>::SMEM_BYTES, stream>>>(tm_dO, tm_V, tm_P, tm_M, tm_dS, \
-                                                                                 prm)
+
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+               const ds::Params);
+  int smem = 0;
   if (rag) {
-    if (prm.resident) ATTN_BWD_LAUNCH_DS(true, true); else ATTN_BWD_LAUNCH_DS(true, false);
+    if (prm.resident) { kern = ds::ds_kernel<true, true>; smem = ds::Cfg<true, true>::SMEM_BYTES; }
+    else { kern = ds::ds_kernel<true, false>; smem = ds::Cfg<true, false>::SMEM_BYTES; }
   } else {
-    if (prm.resident) ATTN_BWD_LAUNCH_DS(false, true); else ATTN_BWD_LAUNCH_DS(false, false);
+    if (prm.resident) { kern = ds::ds_kernel<false, true>; smem = ds::Cfg<false, true>::SMEM_BYTES; }
+    else { kern = ds::ds_kernel<false, false>; smem = ds::Cfg<false, false>::SMEM_BYTES; }
   }
-#undef ATTN_BWD_LAUNCH_DS
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(ds::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  int clusters = st.sm_count;
+  if (prm.cs > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = prm.cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(prm.cs * st.sm_count);
+    int max_clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters < 1)
+      return ATTN_BWD_ECUDA;
+    clusters = max_clusters;
+  }
+  const int n_clusters = prm.n_units < clusters ? prm.n_units : clusters;
+  cfg.gridDim = dim3(n_clusters * prm.cs);
+  if (cudaLaunchKernelEx(&cfg, kern, tm_dO, tm_V, tm_P, tm_M, tm_dS, prm) != cudaSuccess) return ATTN_BWD_ECUDA;
   return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 

@@ -59,7 +59,7 @@ constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 template <bool RAG, bool RES>
 struct Cfg {
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
-  static constexpr int VST = RES ? 2 : 3;              // V chunk stages (non-resident: V read twice)
+  static constexpr int VST = (RES || RAG) ? 2 : 3;   // V chunk stages (aligned non-resident: V read twice)
   static constexpr int PST = RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);  // P/mask chunk stages
   static constexpr int P_PITCH = RAG ? RAG_P_PITCH : 128;  // bytes per staged P row
   static constexpr int M_PITCH = RAG ? RAG_M_PITCH : 64;   // bytes per staged mask row
@@ -77,7 +77,8 @@ struct Cfg {
   static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4;
   static_assert(DOBUF <= 2, "two dO barrier slots");
   static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][4][128]: per-column-group row sums
-  static constexpr int OFF_MISC = OFF_RX + 2 * 4 * BM * 4;
+  static constexpr int OFF_XB = OFF_RX + 2 * 4 * BM * 4;   // float xb[2][8][128]: row sums from each cluster CTA
+  static constexpr int OFF_MISC = OFF_XB + 2 * 8 * BM * 4;   // tmem base, abort flag, cluster exchange barrier
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "dS kernel shared memory");
 };
@@ -87,6 +88,8 @@ struct Params {
   int n_units;      // local (batch·head) count × row blocks
   int n_mb;         // row blocks per head
   int nchunks;      // ceil(skv / 64)
+  int cs;           // CTAs per cluster sharing one unit's columns (1: no cluster)
+  int cpc;          // chunks per CTA of a cluster (CTA k owns chunks [k·cpc, (k+1)·cpc))
   int resident;     // 1: pass 2 re-reads pass-1 TMEM columns
   int bh_base;      // global (batch·head) index of local head 0
   int use_mask;     // p > 0
@@ -188,6 +191,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   float* rx = reinterpret_cast<float*>(smem + C::OFF_RX);
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + C::OFF_MISC + 16);
+  float* xb = reinterpret_cast<float*>(smem + C::OFF_XB);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -202,6 +207,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     }
     for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], kEpiWarps); }
     for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 32 * (kEpiWarps / 4));
+    // every CTA of the cluster (itself included) arrives once per row per unit
+    mbar_init(xbar, prm.cs * BM);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -215,10 +222,19 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   }
   tc_fence_before();
   __syncthreads();
+  if (prm.cs > 1) cluster_sync();   // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
   const int n_units = prm.n_units, n_mb = prm.n_mb, nchunks = prm.nchunks;
+  // Cluster split of long rows: the cs CTAs of a cluster process the same units,
+  // CTA `rank` owning chunks [c0, c0 + nloc) of every row; persistent over units
+  // by cluster.  cs == 1: plain launch, one CTA owns whole rows.
+  const int cs = prm.cs;
+  const int rank = cs > 1 ? int(cluster_ctarank()) : 0;
+  const int cid = int(blockIdx.x) / cs, ncl = int(gridDim.x) / cs;
+  const int c0 = rank * prm.cpc;
+  const int nloc = max(0, min(prm.cpc, nchunks - c0));
   const int sq = prm.sq, skv = prm.skv;
   constexpr bool resident = RES;
   constexpr int npass_mma = RES ? 1 : 2;
@@ -227,7 +243,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   if (warp == 0) {
     // ------------------------------------------------ dO / V producer (lane 0 issues)
     uint32_t vi = 0, di = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       const int bh = prm.bh_base + bhl;
       const int b = bh / kHeads, h = bh - b * kHeads;
@@ -241,7 +257,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       }
       ++di;
       for (int pass = 0; pass < npass_mma; ++pass) {
-        for (int c = 0; c < nchunks; ++c) {
+        for (int cl = 0; cl < nloc; ++cl) {
+          const int c = c0 + cl;
           const int vs = vi % VST;
           if (!warp_wait(&V_empty[vs], ((vi / VST) & 1) ^ 1, abort_flag, err, 0x0102)) goto producer_done;
           if (lane == 0) {
@@ -270,10 +287,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   } else if (warp == 2 || (RAG && warp == 3)) {
     // ------------------------------------------------ P / mask producer (RAG: warps 2 and 3)
     uint32_t pi = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       for (int pass = 0; pass < 2; ++pass) {
-        for (int c = 0; c < nchunks; ++c) {
+        for (int cl = 0; cl < nloc; ++cl) {
+          const int c = c0 + cl;
           const int ps = pi % PST;
           if (!warp_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103)) goto pm_done;
           if constexpr (!RAG) {
@@ -322,12 +340,13 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     // ------------------------------------------------ MMA issuer (lane 0 issues)
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
     uint32_t job = 0, vi = 0, di = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (int u = cid; u < n_units; u += ncl) {
       const int db = di % DOBUF;
       if (!warp_wait(&dO_full[db], (di / DOBUF) & 1, abort_flag, err, 0x0201)) goto mma_done;
       const uint32_t a_base = smem_u32(smem + C::OFF_DO + db * DO_BYTES);
       for (int pass = 0; pass < npass_mma; ++pass) {
-        for (int c = 0; c < nchunks; ++c) {
+        for (int cl = 0; cl < nloc; ++cl) {
+          (void)c0;  // chunk coordinates are not needed by the MMA (V chunk order matches)
           const int slot = job % TSLOTS;
           if (!warp_wait(&T_empty[slot], ((job / TSLOTS) & 1) ^ 1, abort_flag, err, 0x0202)) goto mma_done;
           const int vs = vi % VST;
@@ -364,10 +383,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     // tensor store, and frees the stage once the store has read shared memory.
     if constexpr (!RAG) {
       uint32_t pi = 0, dsr_par = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      for (int u = cid; u < n_units; u += ncl) {
         const int bhl = u / n_mb, mb = u - bhl * n_mb;
-        pi += nchunks;  // pass-1 uses of the stages
-        for (int c = 0; c < nchunks; ++c, ++pi) {
+        pi += nloc;  // pass-1 uses of the stages
+        for (int cl = 0; cl < nloc; ++cl, ++pi) {
+          const int c = c0 + cl;
           const int ps = pi % PST;
           if (!warp_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306)) goto store_done;
           dsr_par ^= 1u << ps;
@@ -394,14 +414,15 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     const float scale = prm.scale;
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
     uint32_t job = 0, pi = 0, it = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       const int s_row = mb * BM + row;
       const unsigned long long row_el = ((unsigned long long)bhl * sq + s_row) * skv;
       const uint32_t job0 = job;
       float acc0 = 0.f, acc1 = 0.f;
       // ---- pass 1: row sums  r = Σ m·dP~·P  (the 1/(1-p) is applied once, below)
-      for (int c = 0; c < nchunks; ++c) {
+      for (int cl = 0; cl < nloc; ++cl) {
+          const int c = c0 + cl;
         const int slot = job % TSLOTS;
         if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0301)) goto epi_done;
         tc_fence_after();
@@ -443,13 +464,32 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         rxb[cg * BM + row] = acc0 + acc1;
         mbar_arrive(&pair_bar[q]);
         if (!warp_wait(&pair_bar[q], it & 1, abort_flag, err, 0x0303)) goto epi_done;
-        r = ((rxb[row] + rxb[BM + row]) + (rxb[2 * BM + row] + rxb[3 * BM + row])) * scale;
+        r = (rxb[row] + rxb[BM + row]) + (rxb[2 * BM + row] + rxb[3 * BM + row]);
       }
+      if (cs > 1) {
+        // ---- cluster: send this CTA's row sums to every CTA (itself included) through
+        // distributed shared memory; column group cg serves ranks cg and cg + 4.
+        const uint32_t slot_addr = smem_u32(xb + ((it & 1) * 8 + rank) * BM + row);
+        const uint32_t bar_addr = smem_u32(xbar);
+#pragma unroll
+        for (int k = cg; k < 8; k += 4) {
+          if (k < cs) {
+            st_cluster_f32(mapa_shared(slot_addr, k), r);
+            mbar_arrive_remote(mapa_shared(bar_addr, k));
+          }
+        }
+        if (!warp_wait_cluster(xbar, it & 1, abort_flag, err, 0x0307)) goto epi_done;
+        const float* xr = xb + (it & 1) * 8 * BM + row;
+        r = 0.f;
+        for (int k = 0; k < cs; ++k) r += xr[k * BM];   // same order on every CTA
+      }
+      r *= scale;
       // ---- pass 2: dS = P · (m·dP~/(1-p) − r)
-      for (int c = 0; c < nchunks; ++c) {
+      for (int cl = 0; cl < nloc; ++cl) {
+          const int c = c0 + cl;
         int slot;
         if (resident) {
-          slot = (job0 + c) % TSLOTS;
+          slot = (job0 + cl) % TSLOTS;
         } else {
           slot = job % TSLOTS;
           if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0304)) goto epi_done;
@@ -520,6 +560,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
 
   tc_fence_before();
   __syncthreads();
+  if (prm.cs > 1) cluster_sync();   // no CTA leaves while a peer may still write into its shared memory
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

@@ -124,6 +124,61 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* 
     if (global_ns() - t0 > kWaitLimitNs) { raise_error(err, code); return; }
 }
 
+// ---------------------------------------------------------------- clusters (distributed shared memory)
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of all CTAs of the cluster (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster, releasing this thread's prior writes.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Warp-uniform bounded wait with cluster-scope acquire (for barriers that other
+// CTAs of the cluster arrive on).
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                                  int code) {
+  bool ok = true;
+  if (!mbar_try_wait_cluster(bar, parity)) {
+    const uint64_t t0 = global_ns();
+    uint32_t n = 0;
+    while (!mbar_try_wait_cluster(bar, parity)) {
+      if (*abort) { ok = false; break; }
+      if ((++n & 31u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+        raise_error(err, code);
+        *abort = 1;
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

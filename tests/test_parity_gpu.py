@@ -94,7 +94,8 @@ def test_sol_shapes_sampled(shape, cuda):
 
 
 @pytest.mark.parametrize("shape", [(1, 1, 16), (1, 1, 1), (1, 3, 1), (1, 127, 48), (1, 129, 64),
-                                   (2, 64, 272), (1, 200, 512), (1, 17, 528), (1, 64, 40)],
+                                   (2, 64, 272), (1, 200, 512), (1, 17, 528), (1, 64, 40),
+                                   (1, 33, 1001), (1, 40, 4160), (1, 9, 4103), (2, 130, 1536)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_edge_shapes(shape, cuda):
     bs, sq, skv = shape
