@@ -30,6 +30,16 @@ std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
 EncodeTiledFn g_encode = nullptr;
 
+bool set_ds_smem() {
+#define ATTN_BWD_SMEM(R, M)                                                                               \
+  (cudaFuncSetAttribute(ds::ds_kernel<R, M>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                        ds::Cfg<R, M>::SMEM_BYTES) == cudaSuccess)
+  return ATTN_BWD_SMEM(false, ds::kRecompute) && ATTN_BWD_SMEM(false, ds::kResident) &&
+         ATTN_BWD_SMEM(false, ds::kTmemP) && ATTN_BWD_SMEM(true, ds::kRecompute) &&
+         ATTN_BWD_SMEM(true, ds::kResident) && ATTN_BWD_SMEM(true, ds::kTmemP);
+#undef ATTN_BWD_SMEM
+}
+
 int device_state(DeviceState** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ATTN_BWD_ECUDA;
@@ -43,14 +53,7 @@ int device_state(DeviceState** out) {
     } else if (major != 10) {
       st.rc = ATTN_BWD_EDEVICE;
     } else if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-               cudaFuncSetAttribute(ds::ds_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ds::Cfg<false, false>::SMEM_BYTES) != cudaSuccess ||
-               cudaFuncSetAttribute(ds::ds_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ds::Cfg<false, true>::SMEM_BYTES) != cudaSuccess ||
-               cudaFuncSetAttribute(ds::ds_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ds::Cfg<true, false>::SMEM_BYTES) != cudaSuccess ||
-               cudaFuncSetAttribute(ds::ds_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ds::Cfg<true, true>::SMEM_BYTES) != cudaSuccess ||
+               !set_ds_smem() ||
                cudaFuncSetAttribute(dv::dv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     dv::Cfg<false>::SMEM_BYTES) != cudaSuccess ||
                cudaFuncSetAttribute(dv::dv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -107,16 +110,15 @@ int check_shape(const Shape& s) {
   return ATTN_BWD_OK;
 }
 
-// Largest chunk count (64 seq_kv columns each) for which the dS kernel keeps a
-// unit's dP~ in TMEM between its two passes instead of recomputing it: all 8
-// chunks of the TMEM ring (seq_kv <= 512).  Measured on B200: resident beats
-// recompute at 6 and 8 chunks even though the next unit's MMAs then wait for
-// the ring.  Tunable with ATTN_BWD_RESIDENT_MAX_CHUNKS (0..8), read once.
-int resident_max_chunks() {
+// Pass-2 mode of the dS kernel, chosen per shape: kTmemP (pass 2 from TMEM only)
+// while a row fits 5 chunks per CTA on clusters of up to 8 CTAs (seq_kv <= 2560),
+// then kResident (up to 8 chunks per CTA, seq_kv <= 4096), then kRecompute.
+// ATTN_BWD_DS_MODE = 0/1/2 forces recompute / resident / TMEM-P where the shape
+// allows it (for measurements), read once.
+int forced_ds_mode() {
   static const int v = [] {
-    const char* e = std::getenv("ATTN_BWD_RESIDENT_MAX_CHUNKS");
-    int x = e ? std::atoi(e) : ds::kResidentMaxChunks;
-    return x < 0 ? 0 : (x > ds::TSLOTS ? ds::TSLOTS : x);
+    const char* e = std::getenv("ATTN_BWD_DS_MODE");
+    return e ? std::atoi(e) : -1;
   }();
   return v;
 }
@@ -163,16 +165,27 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.n_mb = (s.sq + ds::BM - 1) / ds::BM;
   prm.n_units = nbh * prm.n_mb;
   prm.nchunks = (s.skv + ds::BN - 1) / ds::BN;
-  // Rows longer than the TMEM ring (8 chunks = 512 columns) are split over a
-  // cluster of cs <= 8 CTAs so every CTA's column slice stays resident; only rows
-  // beyond 8 x 512 columns fall back to recomputing dP~ in pass 2.
-  prm.cs = 1;
-  prm.cpc = prm.nchunks;
-  if (prm.nchunks > ds::TSLOTS && prm.nchunks <= 8 * ds::TSLOTS && resident_max_chunks() == ds::TSLOTS) {
-    prm.cs = (prm.nchunks + ds::TSLOTS - 1) / ds::TSLOTS;
+  // Rows that do not fit one CTA's TMEM plan are split over a cluster of cs <= 8
+  // CTAs (CTA k owns chunks [k*cpc, (k+1)*cpc)); the CTAs exchange row sums.
+  auto split = [&](int per_cta) {
+    prm.cs = (prm.nchunks + per_cta - 1) / per_cta;
     prm.cpc = (prm.nchunks + prm.cs - 1) / prm.cs;
+  };
+  const int tp_max = ds::Cfg<false, ds::kTmemP>::NSLOT;
+  const int forced = forced_ds_mode();
+  int mode;
+  if (prm.nchunks <= 8 * tp_max && (forced < 0 || forced == ds::kTmemP)) {
+    mode = ds::kTmemP;
+    split(tp_max);
+  } else if (prm.nchunks <= 8 * ds::TSLOTS && forced != ds::kRecompute) {
+    mode = ds::kResident;
+    split(ds::TSLOTS);
+  } else {
+    mode = ds::kRecompute;
+    prm.cs = 1;
+    prm.cpc = prm.nchunks;
   }
-  prm.resident = prm.cpc <= resident_max_chunks() ? 1 : 0;
+  prm.resident = mode != ds::kRecompute;
   prm.bh_base = s.u0 * kGroups;
   prm.use_mask = p > 0.f ? 1 : 0;
   prm.scale = p > 0.f ? 1.0f / (1.0f - p) : 1.0f;
@@ -185,15 +198,20 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.m_end16 = (E + 15) & ~15ull;
 
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
-               const ds::Params);
+               const ds::Params) = nullptr;
   int smem = 0;
-  if (rag) {
-    if (prm.resident) { kern = ds::ds_kernel<true, true>; smem = ds::Cfg<true, true>::SMEM_BYTES; }
-    else { kern = ds::ds_kernel<true, false>; smem = ds::Cfg<true, false>::SMEM_BYTES; }
-  } else {
-    if (prm.resident) { kern = ds::ds_kernel<false, true>; smem = ds::Cfg<false, true>::SMEM_BYTES; }
-    else { kern = ds::ds_kernel<false, false>; smem = ds::Cfg<false, false>::SMEM_BYTES; }
+#define ATTN_BWD_PICK(R, M)                    \
+  if (rag == R && mode == M) {                 \
+    kern = ds::ds_kernel<R, M>;                \
+    smem = ds::Cfg<R, M>::SMEM_BYTES;          \
   }
+  ATTN_BWD_PICK(false, ds::kRecompute)
+  ATTN_BWD_PICK(false, ds::kResident)
+  ATTN_BWD_PICK(false, ds::kTmemP)
+  ATTN_BWD_PICK(true, ds::kRecompute)
+  ATTN_BWD_PICK(true, ds::kResident)
+  ATTN_BWD_PICK(true, ds::kTmemP)
+#undef ATTN_BWD_PICK
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.blockDim = dim3(ds::kThreads);

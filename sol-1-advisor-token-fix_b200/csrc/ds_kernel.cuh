@@ -49,18 +49,30 @@ constexpr int RAG_M_PITCH = 80;    // ragged rows: 64 B of mask row + 16 B of sl
 constexpr int kEpiWarps = 16;                 // 4 per TMEM lane quadrant
 constexpr int CW = BN / (kEpiWarps / 4);      // 16 chunk columns per epilogue thread
 constexpr int kThreads = (4 + kEpiWarps) * 32;
-constexpr int kResidentMaxChunks = TSLOTS;
 constexpr int DO_BYTES = BM * kHeadDim * 2;   // 32 KB (two 64-column SW128 halves)
 constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 
-// Shared-memory plan per mode.  RES (dP~ resident in TMEM between the passes):
-// the MMAs of a unit end with pass 1, so one dO buffer suffices and the freed
-// space buys P/mask stages (bytes in flight are what keep HBM busy).
-template <bool RAG, bool RES>
+// Pass-2 modes.
+//   kRecompute  pass 2 re-issues the MMAs and re-reads P / mask (from L2); rows of any length.
+//   kResident   dP~ stays in TMEM (8 slots of 64 columns), pass 2 re-reads P / mask from L2.
+//   kTmemP      pass 1 writes the masked dP~ (fp32) and P (bf16 pairs) back into TMEM
+//               (96-column slots, <= 5 chunks per CTA), so pass 2 reads TMEM only and the
+//               whole shared-memory ring prefetches pass-1 data from HBM.
+enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2 };
+
+// Shared-memory plan per mode.  With dP~ resident the MMAs of a unit end with
+// pass 1, so one dO buffer suffices and the freed space buys P/mask stages
+// (bytes in flight are what keep HBM busy).
+template <bool RAG, int MODE>
 struct Cfg {
+  static constexpr bool RES = MODE != kRecompute;
+  static constexpr bool TP = MODE == kTmemP;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   static constexpr int VST = (RES || RAG) ? 2 : 3;   // V chunk stages (aligned non-resident: V read twice)
-  static constexpr int PST = RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);  // P/mask chunk stages
+  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);  // P/mask chunk stages
+  static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
+  static constexpr int NSLOT = TP ? 5 : TSLOTS;        // TMEM slots (<= 512 columns)
+  static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
   static constexpr int P_PITCH = RAG ? RAG_P_PITCH : 128;  // bytes per staged P row
   static constexpr int M_PITCH = RAG ? RAG_M_PITCH : 64;   // bytes per staged mask row
   static constexpr int P_BYTES = BM * P_PITCH;
@@ -72,9 +84,10 @@ struct Cfg {
   static constexpr int OFF_P = OFF_V + VST * V_BYTES;
   static constexpr int OFF_M = OFF_P + PST * P_BYTES;
   static constexpr int OFF_STG = OFF_M + PST * M_BYTES;
-  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
+  static constexpr int OFF_DST = OFF_STG + STG_BYTES;
+  static constexpr int OFF_BAR = OFF_DST + DST_BYTES;
   // barriers: dO full/empty (2+2), V full/empty, PM full/empty, dS ready, T full/empty, quad (4)
-  static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4;
+  static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4 + 2;
   static_assert(DOBUF <= 2, "two dO barrier slots");
   static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][4][128]: per-column-group row sums
   static constexpr int OFF_XB = OFF_RX + 2 * 4 * BM * 4;   // float xb[2][8][128]: row sums from each cluster CTA
@@ -163,7 +176,34 @@ __device__ __forceinline__ uint32_t mask_at(const uint32_t (&mx)[4], int e) {
   return __byte_perm(mx[e >> 2], 0u, (e & 3) * 0x1111u);
 }
 
-template <bool RAG, bool RES>
+// Ragged rows: dS of this warp's 32 rows x 16 columns goes out through the
+// warp's transpose buffer, so each 2-byte store instruction writes 2 rows x 32
+// contiguous bytes instead of 32 scattered rows.
+template <int STG_PITCH>
+__device__ __forceinline__ void store_rag_dS_impl(const uint32_t (&o)[8], uint32_t stg, uint32_t lane, const Params& prm,
+                                                  int bhl, int sq, int skv, int mb, int q, int c, int cg) {
+  using namespace sm100;
+  const uint32_t srow = stg + lane * STG_PITCH;
+  sts128(srow, make_uint4(o[0], o[1], o[2], o[3]));
+  sts128(srow + 16, make_uint4(o[4], o[5], o[6], o[7]));
+  __syncwarp();
+  const int col = c * BN + cg * CW + int(lane & 15);
+  const int rows_here = min(32, sq - (mb * BM + q * 32));
+  if (col < skv) {
+    unsigned short* dst =
+        reinterpret_cast<unsigned short*>(prm.dS) + ((unsigned long long)bhl * sq + mb * BM + q * 32) * skv + col;
+    for (int rr = int(lane >> 4); rr < rows_here; rr += 2) {
+      unsigned short val;
+      asm volatile("ld.shared.u16 %0, [%1];" : "=h"(val) : "r"(stg + rr * STG_PITCH + (lane & 15) * 2));
+      dst[(unsigned long long)rr * skv] = val;
+    }
+  }
+  __syncwarp();
+}
+#define store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg) \
+  store_rag_dS_impl<C::STG_PITCH>(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg)
+
+template <bool RAG, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64,1,128,1) SW128
           const __grid_constant__ CUtensorMap tm_V,    // (d, skv, b·8)  box (64,64,1)    SW128
@@ -172,8 +212,10 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const __grid_constant__ CUtensorMap tm_dS,   // (skv, sq, bh)  box (64,128,1)   SW128 (aligned only)
           const Params prm) {
   using namespace sm100;
-  using C = Cfg<RAG, RES>;
+  using C = Cfg<RAG, MODE>;
   constexpr int PST = C::PST, VST = C::VST, DOBUF = C::DOBUF;
+  constexpr bool RES = C::RES, TP = C::TP;
+  constexpr int NSLOT = C::NSLOT, SLOTC = C::SLOTC;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -188,6 +230,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   uint64_t* T_full = dS_ready + PST;
   uint64_t* T_empty = T_full + TSLOTS;
   uint64_t* pair_bar = T_empty + TSLOTS;
+  uint64_t* dS_free = pair_bar + 4;   // kTmemP: dS staging tile free again (store has read it)
   float* rx = reinterpret_cast<float*>(smem + C::OFF_RX);
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
@@ -207,6 +250,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     }
     for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], kEpiWarps); }
     for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 32 * (kEpiWarps / 4));
+    for (int i = 0; i < 2; ++i) mbar_init(&dS_free[i], 1);
     // every CTA of the cluster (itself included) arrives once per row per unit
     mbar_init(xbar, prm.cs * BM);
     *abort_flag = 0;
@@ -289,7 +333,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     uint32_t pi = 0;
     for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
-      for (int pass = 0; pass < 2; ++pass) {
+      for (int pass = 0; pass < (TP ? 1 : 2); ++pass) {
         for (int cl = 0; cl < nloc; ++cl) {
           const int c = c0 + cl;
           const int ps = pi % PST;
@@ -347,14 +391,14 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       for (int pass = 0; pass < npass_mma; ++pass) {
         for (int cl = 0; cl < nloc; ++cl) {
           (void)c0;  // chunk coordinates are not needed by the MMA (V chunk order matches)
-          const int slot = job % TSLOTS;
-          if (!warp_wait(&T_empty[slot], ((job / TSLOTS) & 1) ^ 1, abort_flag, err, 0x0202)) goto mma_done;
+          const int slot = job % NSLOT;
+          if (!warp_wait(&T_empty[slot], ((job / NSLOT) & 1) ^ 1, abort_flag, err, 0x0202)) goto mma_done;
           const int vs = vi % VST;
           if (!warp_wait(&V_full[vs], (vi / VST) & 1, abort_flag, err, 0x0203)) goto mma_done;
           tc_fence_after();
           if (lane == 0) {
             const uint32_t b_base = smem_u32(smem + C::OFF_V + vs * V_BYTES);
-            const uint32_t d_tmem = tmem_base + slot * BN;
+            const uint32_t d_tmem = tmem_base + slot * SLOTC;
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
               // 16 bf16 = 32 B step inside the 128 B swizzle atom; 64-column halves 16 KB / 8 KB apart
@@ -381,7 +425,28 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     // Walks the same P/mask stage sequence as the epilogue; for each pass-2 chunk it
     // waits until all epilogue warps wrote dS over the stage, stores it with one TMA
     // tensor store, and frees the stage once the store has read shared memory.
-    if constexpr (!RAG) {
+    if constexpr (!RAG && TP) {
+      // kTmemP: dS of pass-2 chunk n is written into staging tile n % 2
+      uint32_t n = 0;
+      for (int u = cid; u < n_units; u += ncl) {
+        const int bhl = u / n_mb, mb = u - bhl * n_mb;
+        for (int cl = 0; cl < nloc; ++cl, ++n) {
+          const int c = c0 + cl;
+          const int b = n & 1;
+          if (!warp_wait(&dS_ready[b], (n >> 1) & 1, abort_flag, err, 0x0306)) goto store_done_tp;
+          if (lane == 0) {
+            tma_store_3d(&tm_dS, smem + C::OFF_DST + b * (BM * BN * 2), c * BN, mb * BM, bhl);
+            bulk_commit();
+            bulk_wait_read0();
+            mbar_arrive(&dS_free[b]);
+          }
+          __syncwarp();
+        }
+      }
+    store_done_tp:
+      if (lane == 0) bulk_wait_all0();
+      __syncwarp();
+    } else if constexpr (!RAG) {
       uint32_t pi = 0, dsr_par = 0;
       for (int u = cid; u < n_units; u += ncl) {
         const int bhl = u / n_mb, mb = u - bhl * n_mb;
@@ -413,7 +478,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     const int use_mask = prm.use_mask;
     const float scale = prm.scale;
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
-    uint32_t job = 0, pi = 0, it = 0;
+    uint32_t job = 0, pi = 0, it = 0, dsn = 0;
     for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       const int s_row = mb * BM + row;
@@ -423,11 +488,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       // ---- pass 1: row sums  r = Σ m·dP~·P  (the 1/(1-p) is applied once, below)
       for (int cl = 0; cl < nloc; ++cl) {
           const int c = c0 + cl;
-        const int slot = job % TSLOTS;
-        if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0301)) goto epi_done;
+        const int slot = job % NSLOT;
+        if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0301)) goto epi_done;
         tc_fence_after();
         uint32_t v[16];
-        tmem_ld16(tmem_base + t_lane + slot * BN + cg * CW, v);
+        tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
         tmem_wait_ld();
         if (!resident) {
           tc_fence_before();
@@ -454,9 +519,20 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           }
           acc0 = fmaf(__uint_as_float(v[2 * k]), __uint_as_float((pw[k] << 16) & m0), acc0);
           acc1 = fmaf(__uint_as_float(v[2 * k + 1]), __uint_as_float(pw[k] & 0xFFFF0000u & m1), acc1);
+          if (TP) {
+            v[2 * k] &= m0;
+            v[2 * k + 1] &= m1;
+          }
+        }
+        if constexpr (TP) {
+          // keep what pass 2 needs in TMEM: masked dP~ over the accumulator columns,
+          // P (bf16 pairs) in the slot's last 32 columns
+          tmem_st16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
+          tmem_st8(tmem_base + t_lane + slot * SLOTC + BN + cg * (CW / 2), pw);
         }
         ++pi;
       }
+      if (TP) tmem_wait_st();
       // ---- combine the four column groups of each row (fixed order: deterministic)
       float r;
       {
@@ -485,19 +561,53 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       }
       r *= scale;
       // ---- pass 2: dS = P · (m·dP~/(1-p) − r)
+      if constexpr (TP) {
+        for (int cl = 0; cl < nloc; ++cl, ++dsn) {
+          const int c = c0 + cl;
+          const int slot = (job0 + cl) % NSLOT;
+          uint32_t v[16], pw[8];
+          tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
+          tmem_ld8(tmem_base + t_lane + slot * SLOTC + BN + cg * (CW / 2), pw);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&T_empty[slot]);
+          uint32_t o[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
+            o[k] = pack_bf16x2(p0 * fmaf(__uint_as_float(v[2 * k]), scale, -r),
+                               p1 * fmaf(__uint_as_float(v[2 * k + 1]), scale, -r));
+          }
+          if constexpr (!RAG) {
+            const int b = dsn & 1;
+            if (!warp_wait(&dS_free[b], ((dsn >> 1) & 1) ^ 1, abort_flag, err, 0x0305)) goto epi_done;
+            const uint32_t d_row = smem_u32(smem + C::OFF_DST + b * (BM * BN * 2)) + row * 128;
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+              sts128(d_row + (((cg * 2 + i) ^ (row & 7)) << 4),
+                     make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dS_ready[b]);
+          } else {
+            store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg);
+          }
+        }
+      } else {
       for (int cl = 0; cl < nloc; ++cl) {
           const int c = c0 + cl;
         int slot;
         if (resident) {
-          slot = (job0 + cl) % TSLOTS;
+          slot = (job0 + cl) % NSLOT;
         } else {
-          slot = job % TSLOTS;
-          if (!warp_wait(&T_full[slot], (job / TSLOTS) & 1, abort_flag, err, 0x0304)) goto epi_done;
+          slot = job % NSLOT;
+          if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0304)) goto epi_done;
           tc_fence_after();
           ++job;
         }
         uint32_t v[16];
-        tmem_ld16(tmem_base + t_lane + slot * BN + cg * CW, v);
+        tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -531,27 +641,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         } else {
           __syncwarp();
           if (lane == 0) mbar_arrive(&PM_empty[ps]);
-          // transpose through the warp's buffer: row-per-thread -> column-per-lane,
-          // then each store instruction writes 2 rows x 32 contiguous bytes
-          const uint32_t srow = stg + lane * C::STG_PITCH;
-          sts128(srow, make_uint4(o[0], o[1], o[2], o[3]));
-          sts128(srow + 16, make_uint4(o[4], o[5], o[6], o[7]));
-          __syncwarp();
-          const int col = c * BN + cg * CW + int(lane & 15);
-          const int rows_here = min(32, sq - (mb * BM + q * 32));
-          if (col < skv) {
-            unsigned short* dst = reinterpret_cast<unsigned short*>(prm.dS) +
-                                  ((unsigned long long)bhl * sq + mb * BM + q * 32) * skv + col;
-            for (int rr = int(lane >> 4); rr < rows_here; rr += 2) {
-              unsigned short val;
-              asm volatile("ld.shared.u16 %0, [%1];" : "=h"(val) : "r"(stg + rr * C::STG_PITCH + (lane & 15) * 2));
-              dst[(unsigned long long)rr * skv] = val;
-            }
-          }
-          __syncwarp();
+          store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg);
         }
         ++pi;
       }
+      }  // pass 2 (re-reading P / mask)
       ++it;
     }
   epi_done:
