@@ -110,9 +110,12 @@ int check_shape(const Shape& s) {
   return ATTN_BWD_OK;
 }
 
-// Pass-2 mode of the dS kernel, chosen per shape: kTmemP (pass 2 from TMEM only)
-// while a row fits 5 chunks per CTA on clusters of up to 8 CTAs (seq_kv <= 2560),
-// then kResident (up to 8 chunks per CTA, seq_kv <= 4096), then kRecompute.
+// Pass-2 mode of the dS kernel, chosen per shape from B200 measurements:
+//   ragged rows: kTmemP while a row fits 5 chunks per CTA on clusters of up to 8
+//     CTAs (its pass 2 avoids re-fetching unaligned rows: c2 dS 553 -> 348 us);
+//   aligned rows: kTmemP up to 4 chunks (no cluster), else kResident (6 shared
+//     P/mask stages beat 4 dedicated ones: c1 100 vs 120 us, c4 1886 vs 2138 us);
+//   then kResident on clusters up to 8 x 512 columns, then kRecompute.
 // ATTN_BWD_DS_MODE = 0/1/2 forces recompute / resident / TMEM-P where the shape
 // allows it (for measurements), read once.
 int forced_ds_mode() {
@@ -174,7 +177,8 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   const int tp_max = ds::Cfg<false, ds::kTmemP>::NSLOT;
   const int forced = forced_ds_mode();
   int mode;
-  if (prm.nchunks <= 8 * tp_max && (forced < 0 || forced == ds::kTmemP)) {
+  const bool tp_pref = rag ? prm.nchunks <= 8 * tp_max : prm.nchunks <= 4;
+  if ((forced < 0 && tp_pref) || (forced == ds::kTmemP && prm.nchunks <= 8 * tp_max)) {
     mode = ds::kTmemP;
     split(tp_max);
   } else if (prm.nchunks <= 8 * ds::TSLOTS && forced != ds::kRecompute) {
