@@ -510,13 +510,24 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         if (lane == 0) mbar_arrive(&PM_empty[ps]);
         expand_mask(mw, use_mask, mx);
         const int nvalid = RAG ? min(max(skv - (c * BN + cg * CW), 0), CW) : CW;
+        if (RAG && nvalid < CW) {
+          // last, partial chunk only: columns >= seq_kv hold the next row's bytes
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (e >= nvalid) mw[e >> 2] &= ~(0xFFu << ((e & 3) * 8));
+          if (!use_mask) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) mx[i] = 0;
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (e < nvalid) mx[e >> 2] |= 0xFFu << ((e & 3) * 8);
+          } else {
+            expand_mask(mw, use_mask, mx);
+          }
+        }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
-          if (RAG) {
-            m0 = (2 * k < nvalid) ? m0 : 0u;
-            m1 = (2 * k + 1 < nvalid) ? m1 : 0u;
-          }
+          const uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
           acc0 = fmaf(__uint_as_float(v[2 * k]), __uint_as_float((pw[k] << 16) & m0), acc0);
           acc1 = fmaf(__uint_as_float(v[2 * k + 1]), __uint_as_float(pw[k] & 0xFFFF0000u & m1), acc1);
           if (TP) {

@@ -20,7 +20,7 @@
 //   RAG = true   any seq_kv: P_drop rows are not 16-byte aligned; the producer
 //                fetches each 128-column row segment with an untiled bulk copy
 //                from the 16-byte boundary below it into a padded row (272 B),
-//                and warps 6..9 re-align the bytes in registers and write the
+//                and warps 6..13 re-align the bytes in registers and write the
 //                128B-swizzled MN-major tile the MMA reads (zeroing columns >=
 //                seq_kv and rows >= seq_q).
 #pragma once
@@ -36,7 +36,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
 template <bool RAG>
 struct Cfg {
-  static constexpr int kThreads = RAG ? 352 : 192;   // RAG: + 4 re-align warps + 1 extra raw-row producer
+  static constexpr int kThreads = RAG ? 480 : 192;   // RAG: + 8 re-align warps (6..13) + 1 extra raw-row producer (14)
   static constexpr int ST = RAG ? 4 : 6;               // operand stages
   static constexpr int RST = RAG ? 4 : 0;              // raw P_drop row stages
   static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack (raw_rows_async)
@@ -119,9 +119,9 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
 
   const uint32_t warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 4); }
+    for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 8); }
     // raw_full: one cp.async completion arrive per lane of the two raw-row producer warps
-    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 64); mbar_init(&raw_empty[i], 4); }
+    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 64); mbar_init(&raw_empty[i], 8); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     fence_barrier_init();
@@ -260,7 +260,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
     }
   }
 
-  else if (RAG && warp == 10) {
+  else if (RAG && warp == 14) {
     // second raw-row producer: rows 32..63 of every K chunk (warp 0 does rows 0..31)
     uint32_t ri = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -280,15 +280,15 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
     __syncwarp();
   }
   else if (RAG) {
-    // re-align warps 6..9: thread t handles row r = t % 64 of the chunk and the
-    // 64-column MN block jb = t / 64
+    // re-align warps 6..13: thread t handles row r = t % 64 of the chunk and the
+    // 32-column quarter qt = t / 64 (uniform per warp) of the 128-column tile
     const int t = int(threadIdx.x) - 6 * 32;
-    const int r = t & 63, jb = t >> 6;
+    const int r = t & 63, qt = t >> 6;
     const int sq = prm.sq, skv = prm.skv;
     uint32_t si = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int ul = u / n_jt, jt = u - ul * n_jt;
-      const int nvalid = min(max(skv - (jt * BM + jb * 64), 0), 64);
+      const int nvalid = min(max(skv - (jt * BM + qt * 32), 0), 32);
       for (int g = 0; g < kGroups; ++g) {
         const int bhl = ul * kGroups + g;
         for (int kc = 0; kc < n_kc; ++kc, ++si) {
@@ -296,31 +296,35 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
           if (!warp_wait(&raw_full[rs], (si / RSTD) & 1, abort_flag, err, 0x1401)) goto realign_done;
           if (!warp_wait(&empty[s], ((si / ST) & 1) ^ 1, abort_flag, err, 0x1402)) goto realign_done;
           const int srow = kc * BK + r;
-          uint32_t w[32];
+          uint32_t w[16];
           if (srow < sq) {
             const unsigned long long el = ((unsigned long long)bhl * sq + srow) * skv + (unsigned long long)jt * BM;
-            const uint32_t src = smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES + r * C::RAW_PITCH + jb * 128);
-            uint32_t in[36];
+            const uint32_t src = smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES + r * C::RAW_PITCH + qt * 64);
+            uint32_t in[20];
 #pragma unroll
-            for (int i = 0; i < 9; ++i) {
+            for (int i = 0; i < 5; ++i) {
               const uint4 x = lds128(src + i * 16);
               in[4 * i] = x.x; in[4 * i + 1] = x.y; in[4 * i + 2] = x.z; in[4 * i + 3] = x.w;
             }
-            byte_shift<32>(in, uint32_t(el * 2) & 15u, w);
+            byte_shift<16>(in, uint32_t(el * 2) & 15u, w);
+            if (nvalid < 32) {   // last, partial tile only: columns >= seq_kv belong to the next row
 #pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              if (2 * k >= nvalid) w[k] = 0;
-              else if (2 * k + 1 >= nvalid) w[k] &= 0xFFFFu;
+              for (int k = 0; k < 16; ++k) {
+                if (2 * k >= nvalid) w[k] = 0;
+                else if (2 * k + 1 >= nvalid) w[k] &= 0xFFFFu;
+              }
             }
           } else {
 #pragma unroll
-            for (int k = 0; k < 32; ++k) w[k] = 0;
+            for (int k = 0; k < 16; ++k) w[k] = 0;
           }
           // 128B-swizzled MN-major row: 16-byte chunk k of row r sits at chunk k ^ (r % 8)
-          const uint32_t dst = smem_u32(smem + s * STAGE_BYTES + jb * (A_BYTES / 2) + r * 128);
+          const uint32_t dst = smem_u32(smem + s * STAGE_BYTES + (qt >> 1) * (A_BYTES / 2) + r * 128);
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            sts128(dst + ((k ^ (r & 7)) << 4), make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]));
+          for (int i = 0; i < 4; ++i) {
+            const int k = (qt & 1) * 4 + i;
+            sts128(dst + ((k ^ (r & 7)) << 4), make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]));
+          }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {

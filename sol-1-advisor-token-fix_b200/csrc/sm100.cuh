@@ -65,6 +65,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same test, but a thread whose phase is not complete may be suspended (up to
+// the hint, in ns) until it completes, instead of spinning through issue slots
+// the working warps need.
+constexpr uint32_t kSuspendHintNs = 0x989680u;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -81,10 +96,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           int* err, int code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  uint32_t n = 0;
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity)) {
     if (*abort) return false;
-    if ((++n & 31u) == 0 && global_ns() - t0 > limit_ns) {
+    if (global_ns() - t0 > limit_ns) {
       raise_error(err, code);
       *abort = 1;
       return false;
@@ -168,7 +182,7 @@ __device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity
     uint32_t n = 0;
     while (!mbar_try_wait_cluster(bar, parity)) {
       if (*abort) { ok = false; break; }
-      if ((++n & 31u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      if ((++n & 7u) == 0 && global_ns() - t0 > kWaitLimitNs) {
         raise_error(err, code);
         *abort = 1;
         ok = false;
