@@ -351,6 +351,23 @@ def main():
     t_e2e = max_over_ranks(sum(e2e_ms) / 1e3, world)
     e2e_val = job["total"] * args.e2e_steps / t_e2e / 1e9
 
+    # ---- gather of every rank's dS / dV shard to rank 0 (NCCL point-to-point), timed
+    # separately: it is not part of the per-call kernel time the value reports
+    gather_ms = None
+    if world > 1:
+        from attn_bwd_b200.shard import gather_to_rank0
+        s_, v_ = step()
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record()
+        out = gather_to_rank0(s_, v_, bs, sq, skv)
+        g1.record()
+        torch.cuda.synchronize()
+        gather_ms = max_over_ranks(g0.elapsed_time(g1), world)
+        del out, s_, v_
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, n, secs = cpu_sample(args.config)
@@ -382,6 +399,7 @@ def main():
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e / args.e2e_steps * 1e3, 2)},
             "gpu_launches": 2 * args.steps,
+            "gather_to_rank0_ms": None if gather_ms is None else round(gather_ms, 3),
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
