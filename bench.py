@@ -357,6 +357,7 @@ def main():
     if world > 1:
         from attn_bwd_b200.shard import gather_to_rank0
         s_, v_ = step()
+        gather_to_rank0(s_, v_, bs, sq, skv)   # warm-up: NCCL sets up its P2P channels lazily
         torch.cuda.synchronize()
         torch.distributed.barrier()
         g0 = torch.cuda.Event(enable_timing=True)
