@@ -35,7 +35,10 @@ import torch  # noqa: E402
 
 METRIC = "attn-bwd µs per call and achieved HBM GB/s (% of roofline) at 1/2/4/8 B200"
 CONFIGS = {"c0": (2, 64, 96), "c1": (6, 384, 384), "c2": (12, 301, 467),
-           "c3": (2, 2048, 3072), "c4": (48, 640, 640)}
+           "c3": (2, 2048, 3072), "c4": (48, 640, 640),
+           # profiling stand-in: 4 of c4's 48 batch rows (same kernel mode, ~1 GB), so that
+           # an ncu capture stays small; its DRAM traffic scales to c4 by 48/4
+           "c4s": (4, 640, 640)}
 H, KVH, G, D = 80, 8, 10, 128
 FALLBACK_HBM_GBS = 6650.0
 
@@ -250,6 +253,20 @@ def run_sol_sweep(args):
                       "reference_best_snapshot_geomean_us": 379.11, "shapes": rows}), flush=True)
 
 
+def run_once(args):
+    """Two warm-up rounds then one dS-kernel and one dV-kernel launch on the config."""
+    import attn_bwd_b200 as ab
+    from attn_bwd_b200.generate import generate_input_lowmem
+    bs, sq, skv = CONFIGS[args.config]
+    dO, P, Pd, V, M, p = generate_input_lowmem(bs, sq, skv, 7, device="cuda")
+    for _ in range(3):
+        ab.ds_shard(dO, P, V, M, p, 0, bs * KVH)
+        ab.dv_shard(dO, Pd, V, 0, bs * KVH)
+    torch.cuda.synchronize()
+    assert ab.poll_error() == 0
+    print(json.dumps({"once": args.config, "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -259,6 +276,8 @@ def main():
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--once", action="store_true",
+                    help="one dS-kernel and one dV-kernel call on the config (for ncu), then exit")
     ap.add_argument("--sweep", choices=["sol"], default=None,
                     help="time the 16 SOL-ExecBench shapes instead of the driver line")
     args = ap.parse_args()
@@ -267,6 +286,8 @@ def main():
         return run_reference(args)
     if args.sweep == "sol":
         return run_sol_sweep(args)
+    if args.once:
+        return run_once(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
