@@ -41,6 +41,11 @@ CONFIGS = {"c0": (2, 64, 96), "c1": (6, 384, 384), "c2": (12, 301, 467),
            "c4s": (4, 640, 640)}
 H, KVH, G, D = 80, 8, 10, 128
 FALLBACK_HBM_GBS = 6650.0
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one dS-kernel launch per
+# (batch, kv-head) unit, from the ncu --set full capture of `bench.py --config c4s --once`
+# (c4s = 4 of c4's 48 batch rows, same kernel mode; 677.07 MB over 32 units), scaled by the
+# units a launch processes.  Only used for the c4 workload's roofline line.
+DS_TRAFFIC_PER_UNIT = {"c4": 677.069e6 / 32}
 
 
 def alg_bytes(units, sq, skv):
@@ -410,7 +415,9 @@ def main():
                        "l2": "256 MiB buffer written between timed steps; inputs also exceed L2",
                        "alg_bytes_per_call": job["total"]},
             "roofline": {"bound": "hbm", "kernel": "ds_kernel", "achieved": round(ds_gbs, 1),
-                         "peak": peak, "unit": "GB/s", "frac": round(ds_gbs / peak, 4), "traffic": None,
+                         "peak": peak, "unit": "GB/s", "frac": round(ds_gbs / peak, 4),
+                         "traffic": (round(DS_TRAFFIC_PER_UNIT[args.config] * (u1 - u0))
+                                     if args.config in DS_TRAFFIC_PER_UNIT else None),
                          "peak_kind": peak_kind,
                          "alg_bytes_per_launch": mine["ds"], "us_per_launch": round(t_ds * 1e6, 2)},
             "kernels": {
