@@ -58,7 +58,10 @@ constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 //   kTmemP      pass 1 writes the masked dP~ (fp32) and P (bf16 pairs) back into TMEM
 //               (96-column slots, <= 5 chunks per CTA), so pass 2 reads TMEM only and the
 //               whole shared-memory ring prefetches pass-1 data from HBM.
-enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2 };
+//   kInterleave like kResident, but the epilogue alternates pass-1 chunks of unit i with
+//               pass-2 chunks of unit i-1 (both units TMEM-resident, <= 4 chunks per CTA),
+//               so HBM reads are spread evenly instead of arriving in per-unit bursts.
+enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2, kInterleave = 3 };
 
 // Shared-memory plan per mode.  With dP~ resident the MMAs of a unit end with
 // pass 1, so one dO buffer suffices and the freed space buys P/mask stages
@@ -67,6 +70,7 @@ template <bool RAG, int MODE>
 struct Cfg {
   static constexpr bool RES = MODE != kRecompute;
   static constexpr bool TP = MODE == kTmemP;
+  static constexpr bool ILV = MODE == kInterleave;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   static constexpr int VST = (RES || RAG) ? 2 : 3;   // V chunk stages (aligned non-resident: V read twice)
   static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);  // P/mask chunk stages
@@ -214,7 +218,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   using namespace sm100;
   using C = Cfg<RAG, MODE>;
   constexpr int PST = C::PST, VST = C::VST, DOBUF = C::DOBUF;
-  constexpr bool RES = C::RES, TP = C::TP;
+  constexpr bool RES = C::RES, TP = C::TP, ILV = C::ILV;
+  static_assert(!(ILV && RAG), "interleaved order is built for aligned rows only");
   constexpr int NSLOT = C::NSLOT, SLOTC = C::SLOTC;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -280,7 +285,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   const int c0 = rank * prm.cpc;
   const int nloc = max(0, min(prm.cpc, nchunks - c0));
   const int sq = prm.sq, skv = prm.skv;
-  constexpr bool resident = RES;
   constexpr int npass_mma = RES ? 1 : 2;
   int* err = prm.err;
 
@@ -331,6 +335,29 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   } else if (warp == 2 || (RAG && warp == 3)) {
     // ------------------------------------------------ P / mask producer (RAG: warps 2 and 3)
     uint32_t pi = 0;
+    if constexpr (ILV) {
+      // same interleaved order as the epilogue: [unit i chunk j (pass 1), unit i-1 chunk j (pass 2)]
+      const int nu = n_units > cid ? (n_units - cid + ncl - 1) / ncl : 0;
+      for (int i = 0; i <= nu; ++i) {
+        for (int cl = 0; cl < nloc; ++cl) {
+          for (int w = 0; w < 2; ++w) {
+            const int ii = i - w;
+            if (ii < 0 || ii >= nu) continue;
+            const int u = cid + ii * ncl;
+            const int bhl = u / n_mb, mb = u - bhl * n_mb;
+            const int c = c0 + cl;
+            const int ps = pi % PST;
+            if (!warp_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103)) goto pm_done;
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
+              tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
+              tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
+            }
+            ++pi;
+          }
+        }
+      }
+    } else {
     for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       for (int pass = 0; pass < (TP ? 1 : 2); ++pass) {
@@ -370,6 +397,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           ++pi;
         }
       }
+    }
     }
   pm_done:
     if (RAG) cp_async_wait_all();
@@ -446,6 +474,32 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     store_done_tp:
       if (lane == 0) bulk_wait_all0();
       __syncwarp();
+    } else if constexpr (ILV) {
+      uint32_t pi = 0, dsr_par = 0;
+      const int nu = n_units > cid ? (n_units - cid + ncl - 1) / ncl : 0;
+      for (int i = 0; i <= nu; ++i) {
+        for (int cl = 0; cl < nloc; ++cl) {
+          if (i < nu) ++pi;   // pass-1 item of unit i
+          if (i == 0) continue;
+          const int u = cid + (i - 1) * ncl;
+          const int bhl = u / n_mb, mb = u - bhl * n_mb;
+          const int c = c0 + cl;
+          const int ps = pi % PST;
+          if (!warp_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306)) goto store_done_ilv;
+          dsr_par ^= 1u << ps;
+          if (lane == 0) {
+            tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
+            bulk_commit();
+            bulk_wait_read0();
+            mbar_arrive_cnt(&PM_empty[ps], kEpiWarps);
+          }
+          __syncwarp();
+          ++pi;
+        }
+      }
+    store_done_ilv:
+      if (lane == 0) bulk_wait_all0();
+      __syncwarp();
     } else if constexpr (!RAG) {
       uint32_t pi = 0, dsr_par = 0;
       for (int u = cid; u < n_units; u += ncl) {
@@ -478,84 +532,83 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     const int use_mask = prm.use_mask;
     const float scale = prm.scale;
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
-    uint32_t job = 0, pi = 0, it = 0, dsn = 0;
-    for (int u = cid; u < n_units; u += ncl) {
-      const int bhl = u / n_mb, mb = u - bhl * n_mb;
-      const int s_row = mb * BM + row;
-      const unsigned long long row_el = ((unsigned long long)bhl * sq + s_row) * skv;
-      const uint32_t job0 = job;
-      float acc0 = 0.f, acc1 = 0.f;
-      // ---- pass 1: row sums  r = Σ m·dP~·P  (the 1/(1-p) is applied once, below)
-      for (int cl = 0; cl < nloc; ++cl) {
-          const int c = c0 + cl;
-        const int slot = job % NSLOT;
-        if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0301)) goto epi_done;
-        tc_fence_after();
-        uint32_t v[16];
-        tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
-        tmem_wait_ld();
-        if (!resident) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&T_empty[slot]);
-        }
-        ++job;
-        const int ps = pi % PST;
-        if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) goto epi_done;
-        const unsigned long long el = row_el + (unsigned long long)c * BN;
-        uint32_t pw[8], mw[4], mx[4];
-        load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES),
-                      row, cg, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
+    uint32_t job = 0, pi = 0, dsn = 0;
+
+    // Pass 1 of one chunk: row-sum contribution Σ m·dP~·P (the 1/(1-p) is applied once,
+    // after the exchange).  kTmemP also parks the masked dP~ and P in TMEM for pass 2.
+    auto p1_chunk = [&](unsigned long long row_el, int cl, float& acc0, float& acc1) -> bool {
+      const int c = c0 + cl;
+      const int slot = job % NSLOT;
+      if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0301)) return false;
+      tc_fence_after();
+      uint32_t v[16];
+      tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
+      tmem_wait_ld();
+      if (!RES) {
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&PM_empty[ps]);
-        expand_mask(mw, use_mask, mx);
-        const int nvalid = RAG ? min(max(skv - (c * BN + cg * CW), 0), CW) : CW;
-        if (RAG && nvalid < CW) {
-          // last, partial chunk only: columns >= seq_kv hold the next row's bytes
+        if (lane == 0) mbar_arrive(&T_empty[slot]);
+      }
+      ++job;
+      const int ps = pi % PST;
+      if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) return false;
+      const unsigned long long el = row_el + (unsigned long long)c * BN;
+      uint32_t pw[8], mw[4], mx[4];
+      load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row,
+                    cg, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&PM_empty[ps]);
+      expand_mask(mw, use_mask, mx);
+      const int nvalid = RAG ? min(max(skv - (c * BN + cg * CW), 0), CW) : CW;
+      if (RAG && nvalid < CW) {
+        // last, partial chunk only: columns >= seq_kv hold the next row's bytes
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (e >= nvalid) mw[e >> 2] &= ~(0xFFu << ((e & 3) * 8));
+        if (!use_mask) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mx[i] = 0;
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            if (e >= nvalid) mw[e >> 2] &= ~(0xFFu << ((e & 3) * 8));
-          if (!use_mask) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) mx[i] = 0;
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (e < nvalid) mx[e >> 2] |= 0xFFu << ((e & 3) * 8);
-          } else {
-            expand_mask(mw, use_mask, mx);
-          }
+            if (e < nvalid) mx[e >> 2] |= 0xFFu << ((e & 3) * 8);
+        } else {
+          expand_mask(mw, use_mask, mx);
         }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
-          acc0 = fmaf(__uint_as_float(v[2 * k]), __uint_as_float((pw[k] << 16) & m0), acc0);
-          acc1 = fmaf(__uint_as_float(v[2 * k + 1]), __uint_as_float(pw[k] & 0xFFFF0000u & m1), acc1);
-          if (TP) {
-            v[2 * k] &= m0;
-            v[2 * k + 1] &= m1;
-          }
-        }
-        if constexpr (TP) {
-          // keep what pass 2 needs in TMEM: masked dP~ over the accumulator columns,
-          // P (bf16 pairs) in the slot's last 32 columns
-          tmem_st16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
-          tmem_st8(tmem_base + t_lane + slot * SLOTC + BN + cg * (CW / 2), pw);
-        }
-        ++pi;
       }
-      if (TP) tmem_wait_st();
-      // ---- combine the four column groups of each row (fixed order: deterministic)
-      float r;
-      {
-        float* rxb = rx + (it & 1) * 4 * BM;
-        rxb[cg * BM + row] = acc0 + acc1;
-        mbar_arrive(&pair_bar[q]);
-        if (!warp_wait(&pair_bar[q], it & 1, abort_flag, err, 0x0303)) goto epi_done;
-        r = (rxb[row] + rxb[BM + row]) + (rxb[2 * BM + row] + rxb[3 * BM + row]);
+#ifdef ATTN_BWD_EXPERIMENT_NOMATH
+      if (false)
+#endif
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
+        acc0 = fmaf(__uint_as_float(v[2 * k]), __uint_as_float((pw[k] << 16) & m0), acc0);
+        acc1 = fmaf(__uint_as_float(v[2 * k + 1]), __uint_as_float(pw[k] & 0xFFFF0000u & m1), acc1);
+        if (TP) {
+          v[2 * k] &= m0;
+          v[2 * k + 1] &= m1;
+        }
       }
+      if constexpr (TP) {
+        // keep what pass 2 needs in TMEM: masked dP~ over the accumulator columns,
+        // P (bf16 pairs) in the slot's last 32 columns
+        tmem_st16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
+        tmem_st8(tmem_base + t_lane + slot * SLOTC + BN + cg * (CW / 2), pw);
+      }
+      ++pi;
+      return true;
+    };
+
+    // Row sums of one unit: the four column groups through shared memory (fixed order,
+    // deterministic), then -- on a cluster -- the partials of every CTA through
+    // distributed shared memory; returns r = Σ dP·P including the 1/(1-p).
+    auto exchange = [&](float acc, uint32_t it, float& r) -> bool {
+      float* rxb = rx + (it & 1) * 4 * BM;
+      rxb[cg * BM + row] = acc;
+      mbar_arrive(&pair_bar[q]);
+      if (!warp_wait(&pair_bar[q], it & 1, abort_flag, err, 0x0303)) return false;
+      r = (rxb[row] + rxb[BM + row]) + (rxb[2 * BM + row] + rxb[3 * BM + row]);
       if (cs > 1) {
-        // ---- cluster: send this CTA's row sums to every CTA (itself included) through
-        // distributed shared memory; column group cg serves ranks cg and cg + 4.
+        // column group cg serves cluster ranks cg and cg + 4 (itself included)
         const uint32_t slot_addr = smem_u32(xb + ((it & 1) * 8 + rank) * BM + row);
         const uint32_t bar_addr = smem_u32(xbar);
 #pragma unroll
@@ -565,55 +618,57 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
             mbar_arrive_remote(mapa_shared(bar_addr, k));
           }
         }
-        if (!warp_wait_cluster(xbar, it & 1, abort_flag, err, 0x0307)) goto epi_done;
+        if (!warp_wait_cluster(xbar, it & 1, abort_flag, err, 0x0307)) return false;
         const float* xr = xb + (it & 1) * 8 * BM + row;
         r = 0.f;
         for (int k = 0; k < cs; ++k) r += xr[k * BM];   // same order on every CTA
       }
       r *= scale;
-      // ---- pass 2: dS = P · (m·dP~/(1-p) − r)
+      return true;
+    };
+
+    // Pass 2 of one chunk: dS = P · (m·dP~/(1-p) − r).
+    auto p2_chunk = [&](int bhl, int mb, unsigned long long row_el, int cl, uint32_t job0, float r) -> bool {
+      const int c = c0 + cl;
+      uint32_t o[8];
       if constexpr (TP) {
-        for (int cl = 0; cl < nloc; ++cl, ++dsn) {
-          const int c = c0 + cl;
-          const int slot = (job0 + cl) % NSLOT;
-          uint32_t v[16], pw[8];
-          tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
-          tmem_ld8(tmem_base + t_lane + slot * SLOTC + BN + cg * (CW / 2), pw);
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&T_empty[slot]);
-          uint32_t o[8];
+        const int slot = (job0 + cl) % NSLOT;
+        uint32_t v[16], pw[8];
+        tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
+        tmem_ld8(tmem_base + t_lane + slot * SLOTC + BN + cg * (CW / 2), pw);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&T_empty[slot]);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
-            o[k] = pack_bf16x2(p0 * fmaf(__uint_as_float(v[2 * k]), scale, -r),
-                               p1 * fmaf(__uint_as_float(v[2 * k + 1]), scale, -r));
-          }
-          if constexpr (!RAG) {
-            const int b = dsn & 1;
-            if (!warp_wait(&dS_free[b], ((dsn >> 1) & 1) ^ 1, abort_flag, err, 0x0305)) goto epi_done;
-            const uint32_t d_row = smem_u32(smem + C::OFF_DST + b * (BM * BN * 2)) + row * 128;
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-              sts128(d_row + (((cg * 2 + i) ^ (row & 7)) << 4),
-                     make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dS_ready[b]);
-          } else {
-            store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg);
-          }
+        for (int k = 0; k < 8; ++k) {
+          const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
+          o[k] = pack_bf16x2(p0 * fmaf(__uint_as_float(v[2 * k]), scale, -r),
+                             p1 * fmaf(__uint_as_float(v[2 * k + 1]), scale, -r));
         }
+        if constexpr (!RAG) {
+          const int b = dsn & 1;
+          if (!warp_wait(&dS_free[b], ((dsn >> 1) & 1) ^ 1, abort_flag, err, 0x0305)) return false;
+          const uint32_t d_row = smem_u32(smem + C::OFF_DST + b * (BM * BN * 2)) + row * 128;
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            sts128(d_row + (((cg * 2 + i) ^ (row & 7)) << 4),
+                   make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dS_ready[b]);
+        } else {
+          store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg);
+        }
+        ++dsn;
+        return true;
       } else {
-      for (int cl = 0; cl < nloc; ++cl) {
-          const int c = c0 + cl;
         int slot;
-        if (resident) {
+        if (RES) {
           slot = (job0 + cl) % NSLOT;
         } else {
           slot = job % NSLOT;
-          if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0304)) goto epi_done;
+          if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0304)) return false;
           tc_fence_after();
           ++job;
         }
@@ -624,14 +679,17 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         __syncwarp();
         if (lane == 0) mbar_arrive(&T_empty[slot]);
         const int ps = pi % PST;
-        if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) goto epi_done;
+        if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) return false;
         const unsigned long long el = row_el + (unsigned long long)c * BN;
         const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
         uint32_t pw[8], mw[4], mx[4];
         load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, uint32_t(el * 2) & 15u,
                       uint32_t(el) & 15u, pw, mw);
         expand_mask(mw, use_mask, mx);
-        uint32_t o[8];
+#ifdef ATTN_BWD_EXPERIMENT_NOMATH
+        for (int k = 0; k < 8; ++k) o[k] = pw[k] ^ v[k] ^ mx[k & 3];
+        if (false)
+#endif
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float t0 = __uint_as_float(v[2 * k] & mask_at(mx, 2 * k));
@@ -655,9 +713,46 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg);
         }
         ++pi;
+        return true;
       }
-      }  // pass 2 (re-reading P / mask)
-      ++it;
+    };
+
+    if constexpr (!ILV) {
+      uint32_t it = 0;
+      for (int u = cid; u < n_units; u += ncl, ++it) {
+        const int bhl = u / n_mb, mb = u - bhl * n_mb;
+        const unsigned long long row_el = ((unsigned long long)bhl * sq + mb * BM + row) * skv;
+        const uint32_t job0 = job;
+        float acc0 = 0.f, acc1 = 0.f, r;
+        for (int cl = 0; cl < nloc; ++cl)
+          if (!p1_chunk(row_el, cl, acc0, acc1)) goto epi_done;
+        if (TP) tmem_wait_st();
+        if (!exchange(acc0 + acc1, it, r)) goto epi_done;
+        for (int cl = 0; cl < nloc; ++cl)
+          if (!p2_chunk(bhl, mb, row_el, cl, job0, r)) goto epi_done;
+      }
+    } else {
+      // Interleaved order: step i runs [pass-1 chunk j of unit i, pass-2 chunk j of unit
+      // i-1] for every j, so each step takes one chunk from HBM and one from L2.
+      const int nu = n_units > cid ? (n_units - cid + ncl - 1) / ncl : 0;
+      int prev_bhl = 0, prev_mb = 0;
+      unsigned long long prev_row_el = 0;
+      uint32_t prev_job0 = 0;
+      float prev_r = 0.f;
+      for (int i = 0; i <= nu; ++i) {
+        const int u = cid + i * ncl;
+        const bool has_cur = i < nu, has_prev = i > 0;
+        const int bhl = has_cur ? u / n_mb : 0, mb = has_cur ? u - (u / n_mb) * n_mb : 0;
+        const unsigned long long row_el = ((unsigned long long)bhl * sq + mb * BM + row) * skv;
+        const uint32_t job0 = job;
+        float acc0 = 0.f, acc1 = 0.f, r = 0.f;
+        for (int cl = 0; cl < nloc; ++cl) {
+          if (has_cur && !p1_chunk(row_el, cl, acc0, acc1)) goto epi_done;
+          if (has_prev && !p2_chunk(prev_bhl, prev_mb, prev_row_el, cl, prev_job0, prev_r)) goto epi_done;
+        }
+        if (has_cur && !exchange(acc0 + acc1, uint32_t(i), r)) goto epi_done;
+        prev_bhl = bhl; prev_mb = mb; prev_row_el = row_el; prev_job0 = job0; prev_r = r;
+      }
     }
   epi_done:
     __syncwarp();
