@@ -35,8 +35,7 @@ bool set_ds_smem() {
   (cudaFuncSetAttribute(ds::ds_kernel<R, M>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
                         ds::Cfg<R, M>::SMEM_BYTES) == cudaSuccess)
   return ATTN_BWD_SMEM(false, ds::kRecompute) && ATTN_BWD_SMEM(false, ds::kResident) &&
-         ATTN_BWD_SMEM(false, ds::kTmemP) && ATTN_BWD_SMEM(false, ds::kInterleave) &&
-         ATTN_BWD_SMEM(true, ds::kRecompute) &&
+         ATTN_BWD_SMEM(false, ds::kTmemP) && ATTN_BWD_SMEM(true, ds::kRecompute) &&
          ATTN_BWD_SMEM(true, ds::kResident) && ATTN_BWD_SMEM(true, ds::kTmemP);
 #undef ATTN_BWD_SMEM
 }
@@ -177,29 +176,11 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   };
   const int tp_max = ds::Cfg<false, ds::kTmemP>::NSLOT;
   const int forced = forced_ds_mode();
-  // interleaved order: 2 units resident at once, so <= 4 chunks per CTA; pick the
-  // cluster size (<= 8) trading idle chunk slots (2 per slot) against CTAs per unit
-  // (1 per extra CTA: each reloads the dO tile and joins the row-sum exchange)
-  auto ilv_split = [&]() -> bool {
-    int best = 0, best_cost = 1 << 30;
-    for (int cs = 1; cs <= 8; ++cs) {
-      const int cpc = (prm.nchunks + cs - 1) / cs;
-      if (cpc > ds::TSLOTS / 2) continue;
-      const int cost = 2 * (cs * cpc - prm.nchunks) + (cs - 1);
-      if (cost < best_cost) { best = cs; best_cost = cost; }
-    }
-    if (!best) return false;
-    prm.cs = best;
-    prm.cpc = (prm.nchunks + best - 1) / best;
-    return true;
-  };
   int mode;
-  const bool tp_pref = rag ? prm.nchunks <= 8 * tp_max : false;
+  const bool tp_pref = rag ? prm.nchunks <= 8 * tp_max : false;   // aligned rows: kResident measured faster
   if ((forced < 0 && tp_pref) || (forced == ds::kTmemP && prm.nchunks <= 8 * tp_max)) {
     mode = ds::kTmemP;
     split(tp_max);
-  } else if (!rag && (forced < 0 || forced == ds::kInterleave) && ilv_split()) {
-    mode = ds::kInterleave;
   } else if (prm.nchunks <= 8 * ds::TSLOTS && forced != ds::kRecompute) {
     mode = ds::kResident;
     split(ds::TSLOTS);
@@ -231,7 +212,6 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   ATTN_BWD_PICK(false, ds::kRecompute)
   ATTN_BWD_PICK(false, ds::kResident)
   ATTN_BWD_PICK(false, ds::kTmemP)
-  ATTN_BWD_PICK(false, ds::kInterleave)
   ATTN_BWD_PICK(true, ds::kRecompute)
   ATTN_BWD_PICK(true, ds::kResident)
   ATTN_BWD_PICK(true, ds::kTmemP)

@@ -58,10 +58,7 @@ constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 //   kTmemP      pass 1 writes the masked dP~ (fp32) and P (bf16 pairs) back into TMEM
 //               (96-column slots, <= 5 chunks per CTA), so pass 2 reads TMEM only and the
 //               whole shared-memory ring prefetches pass-1 data from HBM.
-//   kInterleave like kResident, but the epilogue alternates pass-1 chunks of unit i with
-//               pass-2 chunks of unit i-1 (both units TMEM-resident, <= 4 chunks per CTA),
-//               so HBM reads are spread evenly instead of arriving in per-unit bursts.
-enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2, kInterleave = 3 };
+enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2 };
 
 // Shared-memory plan per mode.  With dP~ resident the MMAs of a unit end with
 // pass 1, so one dO buffer suffices and the freed space buys P/mask stages
@@ -70,7 +67,6 @@ template <bool RAG, int MODE>
 struct Cfg {
   static constexpr bool RES = MODE != kRecompute;
   static constexpr bool TP = MODE == kTmemP;
-  static constexpr bool ILV = MODE == kInterleave;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   static constexpr int VST = (RES || RAG) ? 2 : 3;   // V chunk stages (aligned non-resident: V read twice)
   static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);  // P/mask chunk stages
@@ -218,8 +214,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   using namespace sm100;
   using C = Cfg<RAG, MODE>;
   constexpr int PST = C::PST, VST = C::VST, DOBUF = C::DOBUF;
-  constexpr bool RES = C::RES, TP = C::TP, ILV = C::ILV;
-  static_assert(!(ILV && RAG), "interleaved order is built for aligned rows only");
+  constexpr bool RES = C::RES, TP = C::TP;
   constexpr int NSLOT = C::NSLOT, SLOTC = C::SLOTC;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -335,29 +330,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   } else if (warp == 2 || (RAG && warp == 3)) {
     // ------------------------------------------------ P / mask producer (RAG: warps 2 and 3)
     uint32_t pi = 0;
-    if constexpr (ILV) {
-      // same interleaved order as the epilogue: [unit i chunk j (pass 1), unit i-1 chunk j (pass 2)]
-      const int nu = n_units > cid ? (n_units - cid + ncl - 1) / ncl : 0;
-      for (int i = 0; i <= nu; ++i) {
-        for (int cl = 0; cl < nloc; ++cl) {
-          for (int w = 0; w < 2; ++w) {
-            const int ii = i - w;
-            if (ii < 0 || ii >= nu) continue;
-            const int u = cid + ii * ncl;
-            const int bhl = u / n_mb, mb = u - bhl * n_mb;
-            const int c = c0 + cl;
-            const int ps = pi % PST;
-            if (!warp_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103)) goto pm_done;
-            if (lane == 0) {
-              mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
-              tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
-              tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
-            }
-            ++pi;
-          }
-        }
-      }
-    } else {
     for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
       for (int pass = 0; pass < (TP ? 1 : 2); ++pass) {
@@ -397,7 +369,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           ++pi;
         }
       }
-    }
     }
   pm_done:
     if (RAG) cp_async_wait_all();
@@ -474,33 +445,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     store_done_tp:
       if (lane == 0) bulk_wait_all0();
       __syncwarp();
-    } else if constexpr (ILV) {
-      uint32_t pi = 0, dsr_par = 0;
-      const int nu = n_units > cid ? (n_units - cid + ncl - 1) / ncl : 0;
-      for (int i = 0; i <= nu; ++i) {
-        for (int cl = 0; cl < nloc; ++cl) {
-          if (i < nu) ++pi;   // pass-1 item of unit i
-          if (i == 0) continue;
-          const int u = cid + (i - 1) * ncl;
-          const int bhl = u / n_mb, mb = u - bhl * n_mb;
-          const int c = c0 + cl;
-          const int ps = pi % PST;
-          if (!warp_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306)) goto store_done_ilv;
-          dsr_par ^= 1u << ps;
-          if (lane == 0) {
-            tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
-            bulk_commit();
-            bulk_wait_read0();
-            mbar_arrive_cnt(&PM_empty[ps], kEpiWarps);
-          }
-          __syncwarp();
-          ++pi;
-        }
-      }
-    store_done_ilv:
-      if (lane == 0) bulk_wait_all0();
-      __syncwarp();
-    } else if constexpr (!RAG) {
+    } else if constexpr (!RAG
+#ifdef ATTN_BWD_DS_DIRECT_STORE
+                         && false
+#endif
+                         ) {
       uint32_t pi = 0, dsr_par = 0;
       for (int u = cid; u < n_units; u += ncl) {
         const int bhl = u / n_mb, mb = u - bhl * n_mb;
@@ -697,6 +646,18 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
           o[k] = pack_bf16x2(p0 * fmaf(t0, scale, -r), p1 * fmaf(t1, scale, -r));
         }
+#ifdef ATTN_BWD_DS_DIRECT_STORE
+        if constexpr (!RAG) {
+          // each thread writes its row's 16 dS values (one full 32-byte sector) straight to global
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&PM_empty[ps]);
+          if (mb * BM + row < sq && c * BN + cg * CW < skv) {
+            uint4* dst = reinterpret_cast<uint4*>(prm.dS + 2ull * (row_el + (unsigned long long)(c * BN + cg * CW)));
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        } else
+#endif
         if constexpr (!RAG) {
           // dS overwrites P in place (same swizzled positions); warp 3 stores the chunk
           const uint32_t p_row = p_stage + row * 128;
@@ -717,7 +678,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       }
     };
 
-    if constexpr (!ILV) {
+    {
       uint32_t it = 0;
       for (int u = cid; u < n_units; u += ncl, ++it) {
         const int bhl = u / n_mb, mb = u - bhl * n_mb;
@@ -730,28 +691,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         if (!exchange(acc0 + acc1, it, r)) goto epi_done;
         for (int cl = 0; cl < nloc; ++cl)
           if (!p2_chunk(bhl, mb, row_el, cl, job0, r)) goto epi_done;
-      }
-    } else {
-      // Interleaved order: step i runs [pass-1 chunk j of unit i, pass-2 chunk j of unit
-      // i-1] for every j, so each step takes one chunk from HBM and one from L2.
-      const int nu = n_units > cid ? (n_units - cid + ncl - 1) / ncl : 0;
-      int prev_bhl = 0, prev_mb = 0;
-      unsigned long long prev_row_el = 0;
-      uint32_t prev_job0 = 0;
-      float prev_r = 0.f;
-      for (int i = 0; i <= nu; ++i) {
-        const int u = cid + i * ncl;
-        const bool has_cur = i < nu, has_prev = i > 0;
-        const int bhl = has_cur ? u / n_mb : 0, mb = has_cur ? u - (u / n_mb) * n_mb : 0;
-        const unsigned long long row_el = ((unsigned long long)bhl * sq + mb * BM + row) * skv;
-        const uint32_t job0 = job;
-        float acc0 = 0.f, acc1 = 0.f, r = 0.f;
-        for (int cl = 0; cl < nloc; ++cl) {
-          if (has_cur && !p1_chunk(row_el, cl, acc0, acc1)) goto epi_done;
-          if (has_prev && !p2_chunk(prev_bhl, prev_mb, prev_row_el, cl, prev_job0, prev_r)) goto epi_done;
-        }
-        if (has_cur && !exchange(acc0 + acc1, uint32_t(i), r)) goto epi_done;
-        prev_bhl = bhl; prev_mb = mb; prev_row_el = row_el; prev_job0 = job0; prev_r = r;
       }
     }
   epi_done:
