@@ -68,8 +68,15 @@ struct Cfg {
   static constexpr bool RES = MODE != kRecompute;
   static constexpr bool TP = MODE == kTmemP;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
-  static constexpr int VST = (RES || RAG) ? 2 : 3;   // V chunk stages (aligned non-resident: V read twice)
-  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);  // P/mask chunk stages
+#ifndef ATTN_BWD_RES_VST
+#define ATTN_BWD_RES_VST 2
+#endif
+#ifndef ATTN_BWD_RES_PST
+#define ATTN_BWD_RES_PST 6
+#endif
+  // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
+  static constexpr int VST = RAG ? 2 : RES ? (TP ? 2 : ATTN_BWD_RES_VST) : 3;
+  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? ATTN_BWD_RES_PST : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
   static constexpr int NSLOT = TP ? 5 : TSLOTS;        // TMEM slots (<= 512 columns)
   static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
@@ -445,11 +452,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     store_done_tp:
       if (lane == 0) bulk_wait_all0();
       __syncwarp();
-    } else if constexpr (!RAG
-#ifdef ATTN_BWD_DS_DIRECT_STORE
-                         && false
-#endif
-                         ) {
+    } else if constexpr (!RAG) {
       uint32_t pi = 0, dsr_par = 0;
       for (int u = cid; u < n_units; u += ncl) {
         const int bhl = u / n_mb, mb = u - bhl * n_mb;
@@ -646,18 +649,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
           o[k] = pack_bf16x2(p0 * fmaf(t0, scale, -r), p1 * fmaf(t1, scale, -r));
         }
-#ifdef ATTN_BWD_DS_DIRECT_STORE
-        if constexpr (!RAG) {
-          // each thread writes its row's 16 dS values (one full 32-byte sector) straight to global
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&PM_empty[ps]);
-          if (mb * BM + row < sq && c * BN + cg * CW < skv) {
-            uint4* dst = reinterpret_cast<uint4*>(prm.dS + 2ull * (row_el + (unsigned long long)(c * BN + cg * CW)));
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-          }
-        } else
-#endif
         if constexpr (!RAG) {
           // dS overwrites P in place (same swizzled positions); warp 3 stores the chunk
           const uint32_t p_row = p_stage + row * 128;
