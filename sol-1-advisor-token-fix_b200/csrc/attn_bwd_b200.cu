@@ -25,6 +25,11 @@ struct DeviceState {
   int rc = ATTN_BWD_OK;
   int sm_count = 0;
   int* err = nullptr;  // device address of g_kernel_error on this device
+  // Side stream + fork/join events for running the dV kernel next to the dS kernel
+  // (created once per device, on the first full call; never destroyed).
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex side_mu;   // one full call at a time uses the side stream
 };
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
@@ -129,8 +134,15 @@ int forced_ds_mode() {
 // seq_kv rows of P / mask / dS must be 16-byte multiples for the TMA path.
 inline bool tma_rows_ok(int skv) { return (skv % 16) == 0; }
 
+// dv_units_of: CTAs the dV kernel launches for this shape (min(units, SMs)).
+int dv_ctas(const DeviceState& st, const Shape& s) {
+  if (s.n_units() == 0 || s.skv == 0 || s.sq == 0) return 0;
+  const int units = s.n_units() * ((s.skv + dv::BM - 1) / dv::BM);
+  return units < st.sm_count ? units : st.sm_count;
+}
+
 int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void* P, const void* V,
-              const uint8_t* M, float p, void* dS, cudaStream_t stream) {
+              const uint8_t* M, float p, void* dS, cudaStream_t stream, int max_ctas = 0) {
   const int nbh = s.n_units() * kGroups;
   if (nbh == 0 || s.sq == 0 || s.skv == 0) return ATTN_BWD_OK;
   const bool rag = !tma_rows_ok(s.skv);
@@ -221,7 +233,8 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   cfg.blockDim = dim3(ds::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  int clusters = st.sm_count;
+  const int sm_budget = (max_ctas > 0 && max_ctas < st.sm_count) ? max_ctas : st.sm_count;
+  int clusters = sm_budget;
   if (prm.cs > 1) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = prm.cs;
@@ -234,6 +247,7 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
     if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters < 1)
       return ATTN_BWD_ECUDA;
     clusters = max_clusters;
+    if (clusters * prm.cs > sm_budget) clusters = sm_budget / prm.cs > 0 ? sm_budget / prm.cs : 1;
   }
   const int n_clusters = prm.n_units < clusters ? prm.n_units : clusters;
   cfg.gridDim = dim3(n_clusters * prm.cs);
@@ -349,6 +363,29 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
       !aligned16(dV))
     return ATTN_BWD_EALIGN;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  // The dS and dV kernels are independent (different inputs and outputs).  When the dV
+  // kernel needs fewer CTAs than the GPU has SMs, it runs on a side stream next to a dS
+  // grid sized to the remaining SMs (both are persistent, one CTA per SM); the caller's
+  // stream then waits for both.  Otherwise they run back to back on the caller's stream.
+  const int dvc = dv_ctas(*st, s);
+  const int ds_budget = st->sm_count - dvc;
+  if (dvc > 0 && ds_budget >= st->sm_count / 4) {
+    std::lock_guard<std::mutex> lk(st->side_mu);
+    if (!st->side) {
+      if (cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking) != cudaSuccess ||
+          cudaEventCreateWithFlags(&st->fork, cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&st->join, cudaEventDisableTiming) != cudaSuccess)
+        return ATTN_BWD_ECUDA;
+    }
+    if (cudaEventRecord(st->fork, cs) != cudaSuccess || cudaStreamWaitEvent(st->side, st->fork, 0) != cudaSuccess)
+      return ATTN_BWD_ECUDA;
+    const int rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
+    const int rc_ds = rc_dv ? ATTN_BWD_OK : launch_ds(*st, s, dO, P, V, M, p, dS, cs, ds_budget);
+    // join even after an error, so the caller's stream never runs ahead of issued work
+    if (cudaEventRecord(st->join, st->side) != cudaSuccess || cudaStreamWaitEvent(cs, st->join, 0) != cudaSuccess)
+      return ATTN_BWD_ECUDA;
+    return rc_dv ? rc_dv : rc_ds;
+  }
   rc = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
   if (rc) return rc;
   return launch_dv(*st, s, dO, Pd, dV, cs);
