@@ -82,11 +82,8 @@ int device_state(DeviceState** out) {
 }
 
 bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
-              const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw,
-              const cuuint32_t* elem_strides = nullptr) {
+              const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  if (elem_strides)
-    for (int i = 0; i < rank; ++i) estr[i] = elem_strides[i];
   CUresult r = g_encode(m, dt, rank, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -154,12 +151,10 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   std::memset(&tm_M, 0, sizeof(tm_M));
   std::memset(&tm_dS, 0, sizeof(tm_dS));
   {
-    // ragged rows: 16 rows per load, every 8th row of seq_q (class-major unit row order)
     cuuint64_t dims[4] = {kHeadDim, kHeads, (cuuint64_t)s.sq, (cuuint64_t)s.bs};
     cuuint64_t str[3] = {kHeadDim * 2, (cuuint64_t)kHeads * kHeadDim * 2, (cuuint64_t)s.sq * kHeads * kHeadDim * 2};
     cuuint32_t box[4] = {64, 1, ds::BM, 1};
-    cuuint32_t es[4] = {1, 1, rag ? 8u : 1u, 1};
-    if (!make_map(&tm_dO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dO, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, es))
+    if (!make_map(&tm_dO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dO, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return ATTN_BWD_ETMAP;
   }
   {
@@ -178,39 +173,6 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
         !make_map(&tm_dS, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dS, dims, str2, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map(&tm_M, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, M, dims, str1, box, CU_TENSOR_MAP_SWIZZLE_64B))
       return ATTN_BWD_ETMAP;
-  }
-  // Ragged rows: one map per residue class of the flat row index R = head*sq + s.  Rows
-  // of a class are 16*skv bytes apart; the map starts at the class's first row rounded
-  // down to 16 bytes and is exactly as wide as needed to reach that row's end.
-  ds::RagMaps rmaps;
-  std::memset(&rmaps, 0, sizeof(rmaps));
-  if (rag) {
-    const unsigned long long NR = (unsigned long long)nbh * s.sq;
-    for (int c = 0; c < 8; ++c) {
-      const unsigned long long first = (unsigned long long)c * s.skv;        // element index of row c
-      const unsigned long long sh = first & 7ull;
-      const unsigned long long rows = NR > (unsigned long long)c ? (NR - c + 7) / 8 : 0;
-      cuuint64_t dims[2] = {(cuuint64_t)(s.skv + sh), (cuuint64_t)(rows ? rows : 1)};
-      cuuint64_t str[1] = {(cuuint64_t)s.skv * 16};
-      cuuint32_t box[2] = {ds::BN + 8, 16};
-      const void* base = rows ? static_cast<const uint8_t*>(P) + 2 * (first - sh) : P;
-      if (!rows) dims[0] = s.skv;
-      if (!make_map(&rmaps.p[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, str, box,
-                    CU_TENSOR_MAP_SWIZZLE_NONE))
-        return ATTN_BWD_ETMAP;
-    }
-    for (int c = 0; c < 16; ++c) {
-      const unsigned long long first = (unsigned long long)c * s.skv;
-      const unsigned long long sh = first & 15ull;
-      const unsigned long long rows = NR > (unsigned long long)c ? (NR - c + 15) / 16 : 0;
-      cuuint64_t dims[2] = {(cuuint64_t)(s.skv + sh), (cuuint64_t)(rows ? rows : 1)};
-      cuuint64_t str[1] = {(cuuint64_t)s.skv * 16};
-      cuuint32_t box[2] = {ds::BN + 16, 8};
-      const void* base = rows ? M + (first - sh) : M;
-      if (!rows) dims[0] = s.skv;
-      if (!make_map(&rmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
-        return ATTN_BWD_ETMAP;
-    }
   }
   ds::Params prm;
   prm.sq = s.sq;
@@ -252,7 +214,7 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.m_end16 = (E + 15) & ~15ull;
 
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
-               const ds::RagMaps, const ds::Params) = nullptr;
+               const ds::Params) = nullptr;
   int smem = 0;
 #define ATTN_BWD_PICK(R, M)                    \
   if (rag == R && mode == M) {                 \
@@ -289,8 +251,7 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   }
   const int n_clusters = prm.n_units < clusters ? prm.n_units : clusters;
   cfg.gridDim = dim3(n_clusters * prm.cs);
-  if (cudaLaunchKernelEx(&cfg, kern, tm_dO, tm_V, tm_P, tm_M, tm_dS, rmaps, prm) != cudaSuccess)
-    return ATTN_BWD_ECUDA;
+  if (cudaLaunchKernelEx(&cfg, kern, tm_dO, tm_V, tm_P, tm_M, tm_dS, prm) != cudaSuccess) return ATTN_BWD_ECUDA;
   return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 

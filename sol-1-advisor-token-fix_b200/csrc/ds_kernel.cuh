@@ -27,17 +27,12 @@
 // Two row formats (template flag RAG):
 //   RAG = false  seq_kv % 16 == 0: P / mask chunks are TMA tensor tiles
 //                (128B / 64B swizzle) and dS leaves by TMA tensor store.
-//   RAG = true   any seq_kv: rows of P / mask do not start on 16-byte
-//                boundaries, so no single tensor map describes them.  Flat rows
-//                R whose indices differ by 8 (mask: 16) are 16*seq_kv bytes apart,
-//                so each residue class c = R mod 8 (mask: R mod 16) gets its own
-//                tensor map (base rounded down to 16 bytes, box 8 / 16 columns
-//                wider to absorb the shift).  A chunk is 8 P + 16 mask TMA loads
-//                into per-class regions; the MMA row order is permuted to match
-//                (dO tile loaded with a traversal stride of 8 rows, so TMEM lane i
-//                holds unit row 8*(i%16) + i/16).  The epilogue re-aligns each row
-//                in registers (funnel shifts), masks columns >= seq_kv, and stores
-//                dS through a per-warp transpose buffer with 2-byte stores.
+//   RAG = true   any seq_kv: rows of P / mask are not 16-byte aligned, so each
+//                row segment is fetched by its own untiled bulk copy from the
+//                16-byte boundary below it into a padded row (pitch 144 B / 80 B);
+//                the epilogue re-aligns it in registers (funnel shifts), masks
+//                columns >= seq_kv, and stores dS through a per-warp transpose
+//                buffer with coalesced 2-byte stores.
 #pragma once
 #include "sm100.cuh"
 
@@ -49,22 +44,8 @@ namespace ds {
 constexpr int BM = 128;          // rows (seq_q) per unit
 constexpr int BN = 64;           // columns (seq_kv) per chunk
 constexpr int TSLOTS = 8;        // TMEM ring: 8 x 64 fp32 columns = 512
-constexpr int RAG_P_PITCH = 144;   // ragged rows: 128 B of P row + 16 B of misalignment slack (72 columns)
+constexpr int RAG_P_PITCH = 144;   // ragged rows: 128 B of P row + 16 B of misalignment slack
 constexpr int RAG_M_PITCH = 80;    // ragged rows: 64 B of mask row + 16 B of slack
-constexpr int RAG_P_REGION = 16 * RAG_P_PITCH;   // 16 rows of one class mod 8 (2304 B, 128-B aligned)
-constexpr int RAG_M_REGION = 8 * RAG_M_PITCH;    // 8 rows of one class mod 16 (640 B, 128-B aligned)
-
-// Tensor maps of the ragged path: P rows of class c = R mod 8 and mask rows of class R mod 16.
-struct RagMaps {
-  CUtensorMap p[8];
-  CUtensorMap m[16];
-};
-
-// Ragged path: TMEM lane i (unit-internal thread row) holds unit row 8*(i%16) + i/16.
-template <bool RAG>
-__device__ __forceinline__ int unit_row_of_lane(int i) {
-  return RAG ? 8 * (i & 15) + (i >> 4) : i;
-}
 constexpr int kEpiWarps = 16;                 // 4 per TMEM lane quadrant
 constexpr int CW = BN / (kEpiWarps / 4);      // 16 chunk columns per epilogue thread
 constexpr int kThreads = (4 + kEpiWarps) * 32;
@@ -174,17 +155,14 @@ __device__ __forceinline__ void load_row(uint32_t p_stage, uint32_t m_stage, int
     mw[0] = t.x; mw[1] = t.y; mw[2] = t.z; mw[3] = t.w;
   } else {
     uint32_t in[12];
-    // lane row = 16*rho + i' sits in P region rho (rows of class rho mod 8), row i';
-    // its unit row j = 8*i' + rho sits in mask region j % 16, row j / 16
-    const int jrow = unit_row_of_lane<true>(row);
-    const uint32_t p_row = p_stage + (row >> 4) * RAG_P_REGION + (row & 15) * RAG_P_PITCH + cg * 32;
+    const uint32_t p_row = p_stage + row * RAG_P_PITCH + cg * 32;
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
       const uint4 t = lds128(p_row + i * 16);
       in[4 * i] = t.x; in[4 * i + 1] = t.y; in[4 * i + 2] = t.z; in[4 * i + 3] = t.w;
     }
     byte_shift<8>(in, shP, pw);
-    const uint32_t m_row = m_stage + (jrow & 15) * RAG_M_REGION + (jrow >> 4) * RAG_M_PITCH + cg * 16;
+    const uint32_t m_row = m_stage + row * RAG_M_PITCH + cg * 16;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const uint4 t = lds128(m_row + i * 16);
@@ -217,15 +195,14 @@ __device__ __forceinline__ void store_rag_dS_impl(const uint32_t (&o)[8], uint32
   sts128(srow + 16, make_uint4(o[4], o[5], o[6], o[7]));
   __syncwarp();
   const int col = c * BN + cg * CW + int(lane & 15);
+  const int rows_here = min(32, sq - (mb * BM + q * 32));
   if (col < skv) {
-    unsigned short* base = reinterpret_cast<unsigned short*>(prm.dS) + ((unsigned long long)bhl * sq + mb * BM) * skv + col;
-    for (int rr = int(lane >> 4); rr < 32; rr += 2) {
-      // buffer row rr holds TMEM lane 32q + rr, i.e. unit row 8*(rr % 16) + 2q + rr / 16
-      const int j = 8 * (rr & 15) + 2 * q + (rr >> 4);
-      if (mb * BM + j >= sq) continue;
+    unsigned short* dst =
+        reinterpret_cast<unsigned short*>(prm.dS) + ((unsigned long long)bhl * sq + mb * BM + q * 32) * skv + col;
+    for (int rr = int(lane >> 4); rr < rows_here; rr += 2) {
       unsigned short val;
       asm volatile("ld.shared.u16 %0, [%1];" : "=h"(val) : "r"(stg + rr * STG_PITCH + (lane & 15) * 2));
-      base[(unsigned long long)j * skv] = val;
+      dst[(unsigned long long)rr * skv] = val;
     }
   }
   __syncwarp();
@@ -240,7 +217,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const __grid_constant__ CUtensorMap tm_P,    // (skv, sq, bh)  box (64,128,1)   SW128 (aligned rows only)
           const __grid_constant__ CUtensorMap tm_M,    // (skv, sq, bh)  box (64,128,1)   SW64 u8 (aligned only)
           const __grid_constant__ CUtensorMap tm_dS,   // (skv, sq, bh)  box (64,128,1)   SW128 (aligned only)
-          const __grid_constant__ RagMaps rmaps,       // ragged only: per-class P / mask maps
           const Params prm) {
   using namespace sm100;
   using C = Cfg<RAG, MODE>;
@@ -275,7 +251,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     for (int i = 0; i < DOBUF; ++i) { mbar_init(&dO_full[i], 1); mbar_init(&dO_empty[i], 1); }
     for (int i = 0; i < VST; ++i) { mbar_init(&V_full[i], 1); mbar_init(&V_empty[i], 1); }
     for (int i = 0; i < PST; ++i) {
-      mbar_init(&PM_full[i], 1);
+      mbar_init(&PM_full[i], RAG ? 64 : 1);   // RAG: one cp.async completion arrive per producer lane (2 warps)
       mbar_init(&PM_empty[i], kEpiWarps);
       mbar_init(&dS_ready[i], kEpiWarps);
     }
@@ -326,19 +302,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       if (!warp_wait(&dO_empty[db], ((di / DOBUF) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
       if (lane == 0) {
         mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
-        uint8_t* dst = smem + C::OFF_DO + db * DO_BYTES;
-        if constexpr (!RAG) {
-          tma_load_4d(dst, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
-          tma_load_4d(dst + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
-        } else {
-          // class-major row order: 16-row block rho holds unit rows rho, rho+8, ..., rho+120
-          // (the map traverses seq_q with stride 8), matching the per-class P / mask regions
-#pragma unroll 1
-          for (int rho = 0; rho < 8; ++rho) {
-            tma_load_4d(dst + rho * 2048, &tm_dO, &dO_full[db], 0, h, mb * BM + rho, b);
-            tma_load_4d(dst + DO_BYTES / 2 + rho * 2048, &tm_dO, &dO_full[db], 64, h, mb * BM + rho, b);
-          }
-        }
+        tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
+        tma_load_4d(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
       }
       ++di;
       for (int pass = 0; pass < npass_mma; ++pass) {
@@ -369,8 +334,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       }
     }
     __syncwarp();
-  } else if (warp == 2) {
-    // ------------------------------------------------ P / mask producer
+  } else if (warp == 2 || (RAG && warp == 3)) {
+    // ------------------------------------------------ P / mask producer (RAG: warps 2 and 3)
     uint32_t pi = 0;
     for (int u = cid; u < n_units; u += ncl) {
       const int bhl = u / n_mb, mb = u - bhl * n_mb;
@@ -386,30 +351,35 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
               tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
             }
           } else {
-            if (lane == 0) {
-              // per-class tensor maps: region rho takes unit rows rho + 8k (P), sigma + 16k (mask)
-              mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
-              const unsigned long long R0 = (unsigned long long)bhl * sq + (unsigned long long)mb * BM;
-#pragma unroll 1
-              for (int rho = 0; rho < 8; ++rho) {
-                const unsigned long long R = R0 + rho;
-                tma_load_2d(smem + C::OFF_P + ps * C::P_BYTES + rho * RAG_P_REGION, &rmaps.p[R & 7], &PM_full[ps],
-                            c * BN, int(R >> 3));
-              }
-#pragma unroll 1
-              for (int sg = 0; sg < 16; ++sg) {
-                const unsigned long long R = R0 + sg;
-                tma_load_2d(smem + C::OFF_M + ps * C::M_BYTES + sg * RAG_M_REGION, &rmaps.m[R & 15], &PM_full[ps],
-                            c * BN, int(R >> 4));
-              }
+            // 16-byte cp.async of the aligned words covering each row segment: 9 for P,
+            // 5 for the mask.  Warp 2 takes rows 0..63, warp 3 rows 64..127; lane =
+            // (row offset lane/8, word lane%8) so 4 rows go per step and the row start
+            // advances by an add.  Words past the tensor's end (rounded up to 16 bytes)
+            // are skipped; their columns are masked by the consumers.
+            const uint32_t pdst = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
+            const uint32_t mdst = smem_u32(smem + C::OFF_M + ps * C::M_BYTES);
+            const int w = int(lane & 7);
+            const int r0 = (warp == 2 ? 0 : BM / 2) + int(lane >> 3);
+            const int rows = min(BM / 2, sq - mb * BM - (warp == 2 ? 0 : BM / 2));
+            unsigned long long el = ((unsigned long long)bhl * sq + mb * BM + r0) * skv + (unsigned long long)c * BN;
+            const unsigned long long step = 4ull * skv;
+            for (int k = 0; 4 * k + int(lane >> 3) < rows; ++k, el += step) {
+              const int r = r0 + 4 * k;
+              const unsigned long long sp = ((el * 2) & ~15ull) + 16ull * w;
+              const unsigned long long sm_ = (el & ~15ull) + 16ull * w;
+              if (sp < prm.p_end16) cp_async16(pdst + r * C::P_PITCH + w * 16, prm.P + sp);
+              if (w == 0 && sp + 128 < prm.p_end16) cp_async16(pdst + r * C::P_PITCH + 128, prm.P + sp + 128);
+              if (w < 5 && sm_ < prm.m_end16) cp_async16(mdst + r * C::M_PITCH + w * 16, prm.M + sm_);
             }
+            cp_async_arrive_noinc(&PM_full[ps]);
           }
           ++pi;
         }
       }
     }
   pm_done:
-    if (lane == 0) {
+    if (RAG) cp_async_wait_all();
+    if (lane == 0 && warp == 2) {
       for (uint32_t k = 0; k < uint32_t(PST) && k < pi; ++k) {
         const uint32_t i = pi - 1 - k;
         mbar_drain(&PM_full[i % PST], (i / PST) & 1, err, 0x0113);
@@ -703,8 +673,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       uint32_t it = 0;
       for (int u = cid; u < n_units; u += ncl, ++it) {
         const int bhl = u / n_mb, mb = u - bhl * n_mb;
-        const unsigned long long row_el =
-            ((unsigned long long)bhl * sq + mb * BM + unit_row_of_lane<RAG>(row)) * skv;
+        const unsigned long long row_el = ((unsigned long long)bhl * sq + mb * BM + row) * skv;
         const uint32_t job0 = job;
         float acc0 = 0.f, acc1 = 0.f, r;
         for (int cl = 0; cl < nloc; ++cl)
