@@ -95,7 +95,7 @@ def test_sol_shapes_sampled(shape, cuda):
 
 @pytest.mark.parametrize("shape", [(1, 1, 16), (1, 1, 1), (1, 3, 1), (1, 127, 48), (1, 129, 64),
                                    (2, 64, 272), (1, 200, 512), (1, 17, 528), (1, 64, 40),
-                                   (1, 33, 1001), (1, 40, 4160), (1, 9, 4103), (2, 130, 1536)],
+                                   (1, 33, 1001), (1, 40, 4160), (1, 9, 4103), (2, 130, 1536), (1, 20, 3001)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_edge_shapes(shape, cuda):
     bs, sq, skv = shape
@@ -166,3 +166,41 @@ def test_bounded_wait_reports_and_recovers(cuda):
     assert ab.poll_error() == 0x7001
     assert ab.poll_error() == 0          # cleared by the poll
     _check_full(generate_input(1, 16, 64, 8), cuda)
+
+
+_MODE_SCRIPT = r"""
+import sys, torch
+sys.path[:0] = [{root!r}, {pkg!r}]
+import attn_bwd_b200 as ab
+from attn_bwd_b200.generate import generate_input
+from oracle.attn_bwd_oracle import attn_bwd_reference
+bad = []
+for shape in {shapes!r}:
+    data = generate_input(*shape, seed=31)
+    dS, dV = ab.custom_kernel(tuple(t.cuda() if isinstance(t, torch.Tensor) else t for t in data))
+    torch.cuda.synchronize()
+    rS, rV = attn_bwd_reference(data)
+    ok = (torch.allclose(rS.float(), dS.float().cpu(), rtol=1e-2, atol=1e-2) and
+          torch.allclose(rV.float(), dV.float().cpu(), rtol=1e-2, atol=1e-2) and ab.poll_error() == 0)
+    if not ok:
+        bad.append(shape)
+print("BAD" if bad else "OK", bad)
+"""
+
+
+@pytest.mark.parametrize("mode", ["0", "1", "2"])
+def test_every_ds_mode(mode, cuda):
+    """Each pass-2 mode of the dS kernel (recompute / resident / TMEM-held P), forced
+    through ATTN_BWD_DS_MODE where the shape allows it, aligned and ragged rows, with and
+    without clusters, against the oracle (the variable is read once per process, hence
+    the subprocess)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    shapes = [(1, 100, 192), (1, 70, 640), (1, 40, 1280), (1, 33, 467), (1, 21, 901), (1, 17, 3001)]
+    code = _MODE_SCRIPT.format(root=root, pkg=os.path.join(root, "sol-1-advisor-token-fix_b200"), shapes=shapes)
+    env = dict(os.environ, ATTN_BWD_DS_MODE=mode)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip().startswith("OK"), r.stdout
