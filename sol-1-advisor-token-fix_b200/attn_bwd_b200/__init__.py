@@ -113,9 +113,63 @@ def attn_bwd_shard(data, unit_begin, unit_end, out=None):
     return dS, dV
 
 
+_BF16 = torch.bfloat16
+
+
+def _fast_ok(dO, P, Pd, V, M):
+    """True when the inputs need no conversion: CUDA tensors of the right dtypes and
+    shapes, contiguous, 16-byte aligned, on one device (checked cheaply, per call)."""
+    try:
+        if not (dO.is_cuda and dO.dtype is _BF16 and P.dtype is _BF16 and Pd.dtype is _BF16 and
+                V.dtype is _BF16 and M.dtype is torch.bool):
+            return False
+        bs, sq, h, d = dO.shape
+        skv = V.shape[2]
+        if (h != NUM_ATTENTION_HEADS or d != HEAD_DIM or
+                V.shape != (bs, NUM_KEY_VALUE_HEADS, skv, HEAD_DIM) or
+                P.shape != (bs, NUM_ATTENTION_HEADS, sq, skv) or Pd.shape != P.shape or M.shape != P.shape):
+            return False
+        dev = dO.device
+        for t in (P, Pd, V, M):
+            if t.device != dev:
+                return False
+        for t in (dO, P, Pd, V, M):
+            if not t.is_contiguous() or t.data_ptr() & 15:
+                return False
+        return True
+    except (AttributeError, ValueError, TypeError):
+        return False
+
+
+try:
+    _raw_stream = torch._C._cuda_getCurrentRawStream   # int handle of the current stream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
+def _stream_handle(device_index):
+    if _raw_stream is not None:
+        return _raw_stream(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
 def attn_bwd(data, out=None):
     """Full call; returns fresh (dS [bs,80,sq,skv], dV [bs,8,skv,128]) bf16 tensors
     unless ``out`` supplies preallocated ones."""
+    dO, P, Pd, V, M, p = data
+    if out is None and _fast_ok(dO, P, Pd, V, M):
+        idx = dO.device.index
+        if idx != torch.cuda.current_device():
+            with torch.cuda.device(idx):
+                return attn_bwd(data)
+        dS = torch.empty_like(P)
+        dV = torch.empty_like(V)
+        bs, sq = dO.shape[0], dO.shape[1]
+        rc = _lib.fast_fn()(dO.data_ptr(), P.data_ptr(), Pd.data_ptr(), V.data_ptr(), M.data_ptr(), float(p),
+                            bs, sq, V.shape[2], dS.data_ptr(), dV.data_ptr(), _stream_handle(idx))
+        if rc:
+            raise AttnBwdError("attn_bwd_b200", rc)
+        return dS, dV
     dO, P, Pd, V, M, p, bs, sq, skv, u0, u1 = _check_inputs(data)
     with torch.cuda.device(dO.device):
         if out is None:

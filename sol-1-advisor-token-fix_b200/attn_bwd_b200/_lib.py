@@ -55,6 +55,11 @@ def load():
     return _lib
 
 
+def fast_fn():
+    """The bound attn_bwd_b200 entry point (loads the library on first use)."""
+    return load().attn_bwd_b200
+
+
 def strerror(code):
     return load().attn_bwd_b200_strerror(int(code)).decode()
 

@@ -28,6 +28,10 @@ struct DeviceState {
   // Side stream + fork/join events for running the dV kernel next to the dS kernel
   // (created once per device, on the first full call; never destroyed).
   cudaStream_t side = nullptr;
+  // cudaOccupancyMaxActiveClusters per (dS kernel instance, cluster size), filled on first use
+  struct OccEntry { const void* kern; int cs; int clusters; };
+  OccEntry occ[32] = {};
+  int n_occ = 0;
   cudaEvent_t fork = nullptr, join = nullptr;
   std::mutex side_mu;   // one full call at a time uses the side stream
 };
@@ -244,8 +248,17 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
     cfg.numAttrs = 1;
     cfg.gridDim = dim3(prm.cs * st.sm_count);
     int max_clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters < 1)
-      return ATTN_BWD_ECUDA;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      DeviceState& mst = const_cast<DeviceState&>(st);
+      for (int i = 0; i < mst.n_occ; ++i)
+        if (mst.occ[i].kern == (const void*)kern && mst.occ[i].cs == prm.cs) max_clusters = mst.occ[i].clusters;
+      if (!max_clusters) {
+        if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters < 1)
+          return ATTN_BWD_ECUDA;
+        if (mst.n_occ < 32) mst.occ[mst.n_occ++] = {(const void*)kern, prm.cs, max_clusters};
+      }
+    }
     clusters = max_clusters;
     if (clusters * prm.cs > sm_budget) clusters = sm_budget / prm.cs > 0 ? sm_budget / prm.cs : 1;
   }
