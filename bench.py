@@ -232,7 +232,8 @@ SOL_SHAPES = [(4, 256, 256), (8, 373, 449), (4, 1024, 2048), (64, 128, 128), (2,
 def run_sol_sweep(args):
     """The 16 SOL-ExecBench shapes (eval_modal_attn_bwd.py:18-35, sizes only), each timed
     the way the reference evaluator does (eval_modal_attn_bwd.py:365-401): warm-up calls,
-    then L2 flush (256 MiB fill) + CUDA events around custom_kernel per rep.  Prints one
+    then per rep an L2 flush (256 MiB fill), a synchronize, and CUDA events around
+    custom_kernel (so host-side time of the call counts, as it does there).  Prints one
     JSON line with per-shape µs, the geomean and the reference's score 756/geomean."""
     import math
     import attn_bwd_b200 as ab
@@ -246,7 +247,17 @@ def run_sol_sweep(args):
         for _ in range(max(args.warmup, 3)):
             ab.custom_kernel(data)
         torch.cuda.synchronize()
-        ms = timed_loop(lambda: ab.custom_kernel(data), args.steps, flush, stream)
+        ms = []
+        for _ in range(args.steps):   # as the evaluator does: flush, synchronize, events around the call
+            flush.fill_(42)
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ab.custom_kernel(data)
+            e1.record()
+            torch.cuda.synchronize()
+            ms.append(e0.elapsed_time(e1))
         us = sum(ms) / len(ms) * 1e3
         gbs = alg_bytes(bs * KVH, sq, skv)["total"] / (us * 1e-6) / 1e9
         rows.append({"bs": bs, "sq": sq, "skv": skv, "us": round(us, 2), "GBps": round(gbs, 1)})
