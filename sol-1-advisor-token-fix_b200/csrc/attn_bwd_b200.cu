@@ -382,7 +382,8 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
   // stream then waits for both.  Otherwise they run back to back on the caller's stream.
   const int dvc = dv_ctas(*st, s);
   const int ds_budget = st->sm_count - dvc;
-  if (dvc > 0 && ds_budget >= st->sm_count / 4) {
+  static const bool side_on = std::getenv("ATTN_BWD_NO_SIDE_STREAM") == nullptr;
+  if (side_on && dvc > 0 && ds_budget >= st->sm_count / 4) {
     std::lock_guard<std::mutex> lk(st->side_mu);
     if (!st->side) {
       if (cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking) != cudaSuccess ||
