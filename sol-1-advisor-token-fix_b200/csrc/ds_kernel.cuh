@@ -441,19 +441,27 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const int b = n & 1;
           if (!warp_wait(&dS_ready[b], (n >> 1) & 1, abort_flag, err, 0x0306)) goto store_done_tp;
           if (lane == 0) {
+            // one store may stay in flight while the epilogue fills the other staging tile
             tma_store_3d(&tm_dS, smem + C::OFF_DST + b * (BM * BN * 2), c * BN, mb * BM, bhl);
             bulk_commit();
-            bulk_wait_read0();
-            mbar_arrive(&dS_free[b]);
+            if (n > 0) {
+              bulk_wait_read<1>();
+              mbar_arrive(&dS_free[b ^ 1]);
+            }
           }
           __syncwarp();
         }
       }
     store_done_tp:
-      if (lane == 0) bulk_wait_all0();
+      if (lane == 0) {
+        bulk_wait_read0();
+        if (n > 0) mbar_arrive(&dS_free[(n - 1) & 1]);
+        bulk_wait_all0();
+      }
       __syncwarp();
     } else if constexpr (!RAG) {
       uint32_t pi = 0, dsr_par = 0;
+      int npend = 0, pend0 = 0, pend1 = 0;   // stages whose store may still be reading (lane 0)
       for (int u = cid; u < n_units; u += ncl) {
         const int bhl = u / n_mb, mb = u - bhl * n_mb;
         pi += nloc;  // pass-1 uses of the stages
@@ -463,16 +471,32 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           if (!warp_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306)) goto store_done;
           dsr_par ^= 1u << ps;
           if (lane == 0) {
+            // keep up to two stores in flight: a stage is freed once its store has read it
             tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
             bulk_commit();
-            bulk_wait_read0();
-            mbar_arrive_cnt(&PM_empty[ps], kEpiWarps);
+            if (npend == 2) {
+              bulk_wait_read<2>();
+              mbar_arrive_cnt(&PM_empty[pend0], kEpiWarps);
+              pend0 = pend1;
+              pend1 = ps;
+            } else if (npend == 1) {
+              pend1 = ps;
+              npend = 2;
+            } else {
+              pend0 = ps;
+              npend = 1;
+            }
           }
           __syncwarp();
         }
       }
     store_done:
-      if (lane == 0) bulk_wait_all0();
+      if (lane == 0) {
+        bulk_wait_read0();
+        if (npend >= 1) mbar_arrive_cnt(&PM_empty[pend0], kEpiWarps);
+        if (npend == 2) mbar_arrive_cnt(&PM_empty[pend1], kEpiWarps);
+        bulk_wait_all0();
+      }
       __syncwarp();
     }
   } else {
