@@ -489,6 +489,14 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           }
           __syncwarp();
         }
+        // the next unit's pass 1 may need every stage: release this unit's last stores now
+        if (lane == 0 && npend > 0) {
+          bulk_wait_read0();
+          mbar_arrive_cnt(&PM_empty[pend0], kEpiWarps);
+          if (npend == 2) mbar_arrive_cnt(&PM_empty[pend1], kEpiWarps);
+          npend = 0;
+        }
+        __syncwarp();
       }
     store_done:
       if (lane == 0) {
