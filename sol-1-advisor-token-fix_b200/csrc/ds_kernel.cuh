@@ -68,15 +68,9 @@ struct Cfg {
   static constexpr bool RES = MODE != kRecompute;
   static constexpr bool TP = MODE == kTmemP;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
-#ifndef ATTN_BWD_RES_VST
-#define ATTN_BWD_RES_VST 2
-#endif
-#ifndef ATTN_BWD_RES_PST
-#define ATTN_BWD_RES_PST 6
-#endif
   // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
-  static constexpr int VST = RAG ? 2 : RES ? (TP ? 2 : ATTN_BWD_RES_VST) : 3;
-  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? ATTN_BWD_RES_PST : 4);
+  static constexpr int VST = RAG ? 2 : RES ? (TP ? 2 : 2) : 3;
+  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
   static constexpr int NSLOT = TP ? 5 : TSLOTS;        // TMEM slots (<= 512 columns)
   static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
@@ -559,9 +553,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           expand_mask(mw, use_mask, mx);
         }
       }
-#ifdef ATTN_BWD_EXPERIMENT_NOMATH
-      if (false)
-#endif
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
@@ -670,10 +661,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, uint32_t(el * 2) & 15u,
                       uint32_t(el) & 15u, pw, mw);
         expand_mask(mw, use_mask, mx);
-#ifdef ATTN_BWD_EXPERIMENT_NOMATH
-        for (int k = 0; k < 8; ++k) o[k] = pw[k] ^ v[k] ^ mx[k & 3];
-        if (false)
-#endif
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float t0 = __uint_as_float(v[2 * k] & mask_at(mx, 2 * k));
