@@ -79,19 +79,16 @@ struct Cfg {
   static constexpr int P_BYTES = BM * P_PITCH;
   static constexpr int M_BYTES = BM * M_PITCH;
   static constexpr int STG_PITCH = 48;                 // per-warp dS transpose rows (RAG): 32 B + pad
-  static constexpr int STG_BYTES = (RAG && !TP) ? kEpiWarps * 32 * STG_PITCH : 0;
-  // RAG + kTmemP: dS staged in each row's own byte alignment (144-byte rows), two buffers
-  static constexpr int DSR_BYTES = (RAG && TP) ? BM * RAG_P_PITCH : 0;
+  static constexpr int STG_BYTES = RAG ? kEpiWarps * 32 * STG_PITCH : 0;
   static constexpr int OFF_DO = 0;
   static constexpr int OFF_V = OFF_DO + DOBUF * DO_BYTES;
   static constexpr int OFF_P = OFF_V + VST * V_BYTES;
   static constexpr int OFF_M = OFF_P + PST * P_BYTES;
   static constexpr int OFF_STG = OFF_M + PST * M_BYTES;
   static constexpr int OFF_DST = OFF_STG + STG_BYTES;
-  static constexpr int OFF_DSR = OFF_DST + DST_BYTES;
-  static constexpr int OFF_BAR = OFF_DSR + 2 * DSR_BYTES;
+  static constexpr int OFF_BAR = OFF_DST + DST_BYTES;
   // barriers: dO full/empty (2+2), V full/empty, PM full/empty, dS ready, T full/empty, quad (4)
-  static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4 + 2 + 8;
+  static constexpr int NBAR = 4 + 2 * VST + 3 * PST + 2 * TSLOTS + 4 + 2;
   static_assert(DOBUF <= 2, "two dO barrier slots");
   static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][4][128]: per-column-group row sums
   static constexpr int OFF_XB = OFF_RX + 2 * 4 * BM * 4;   // float xb[2][8][128]: row sums from each cluster CTA
@@ -235,7 +232,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   uint64_t* T_empty = T_full + TSLOTS;
   uint64_t* pair_bar = T_empty + TSLOTS;
   uint64_t* dS_free = pair_bar + 4;   // kTmemP: dS staging tile free again (store has read it)
-  uint64_t* qbar = dS_free + 2;       // RAG + kTmemP: [buffer][quadrant] staged dS rows complete
   float* rx = reinterpret_cast<float*>(smem + C::OFF_RX);
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
@@ -256,7 +252,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], kEpiWarps); }
     for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 32 * (kEpiWarps / 4));
     for (int i = 0; i < 2; ++i) mbar_init(&dS_free[i], 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&qbar[i], 32 * (kEpiWarps / 4));
     // every CTA of the cluster (itself included) arrives once per row per unit
     mbar_init(xbar, prm.cs * BM);
     *abort_flag = 0;
@@ -638,49 +633,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           __syncwarp();
           if (lane == 0) mbar_arrive(&dS_ready[b]);
         } else {
-          // stage the 16 values in the row's own alignment, then (after the quadrant's four
-          // column-group warps are done) write whole 16-byte words; 2 buffers by chunk parity
-          const int b = dsn & 1;
-          const uint32_t qbase = smem_u32(smem + C::OFF_DSR) + b * C::DSR_BYTES + q * 32 * RAG_P_PITCH;
-          const unsigned long long el = row_el + (unsigned long long)c * BN;
-          const uint32_t sh = uint32_t(el * 2) & 15u;
-          const uint32_t wrow = qbase + lane * RAG_P_PITCH + sh + cg * 32;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            asm volatile("st.shared.b16 [%0], %1;" ::"r"(wrow + 4 * k), "h"((unsigned short)(o[k] & 0xFFFFu)) : "memory");
-            asm volatile("st.shared.b16 [%0], %1;" ::"r"(wrow + 4 * k + 2), "h"((unsigned short)(o[k] >> 16)) : "memory");
-          }
-          mbar_arrive(&qbar[b * 4 + q]);
-          if (!warp_wait(&qbar[b * 4 + q], (dsn >> 1) & 1, abort_flag, err, 0x0308)) return false;
-          // this warp writes rows cg*8 .. cg*8+7 of the quadrant: 8 lanes per row, lane%8 = word
-          const int bytes = 2 * min(BN, skv - c * BN);
-          uint8_t* gbase = prm.dS;
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int rl = cg * 8 + half * 4 + int(lane >> 3);
-            const int s_abs = mb * BM + q * 32 + rl;
-            if (s_abs >= sq) continue;
-            const unsigned long long g0 = 2ull * (((unsigned long long)bhl * sq + s_abs) * skv + (unsigned long long)c * BN);
-            const unsigned long long a0 = g0 & ~15ull, g1 = g0 + bytes;
-            const uint32_t src = qbase + rl * RAG_P_PITCH;
-            for (int w = int(lane & 7); w < 9; w += 8) {
-              const unsigned long long ws = a0 + 16ull * w;
-              if (ws >= g1) break;
-              if (ws >= g0 && ws + 16 <= g1) {
-                const uint4 v4 = lds128(src + 16 * w);
-                *reinterpret_cast<uint4*>(gbase + ws) = v4;
-              } else {
-                for (int e = 0; e < 8; ++e) {
-                  const unsigned long long ga = ws + 2 * e;
-                  if (ga >= g0 && ga < g1) {
-                    unsigned short val;
-                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(val) : "r"(src + 16 * w + 2 * e));
-                    *reinterpret_cast<unsigned short*>(gbase + ga) = val;
-                  }
-                }
-              }
-            }
-          }
+          store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg);
         }
         ++dsn;
         return true;
