@@ -376,14 +376,16 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
       !aligned16(dV))
     return ATTN_BWD_EALIGN;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  // The dS and dV kernels are independent (different inputs and outputs).  When the dV
-  // kernel needs fewer CTAs than the GPU has SMs, it runs on a side stream next to a dS
-  // grid sized to the remaining SMs (both are persistent, one CTA per SM); the caller's
-  // stream then waits for both.  Otherwise they run back to back on the caller's stream.
+  // The dS and dV kernels are independent (different inputs and outputs), so the dV
+  // kernel always runs on a side stream forked from the caller's stream, which waits for
+  // both at the end.  When dV needs fewer CTAs than SMs, the dS grid is sized to the
+  // remaining SMs and both run side by side (dV launched first); otherwise dS is launched
+  // first with the full grid and dV's CTAs take over SMs as dS CTAs finish, filling the
+  // dS kernel's tail.  ATTN_BWD_NO_SIDE_STREAM=1 runs them back to back on one stream.
   const int dvc = dv_ctas(*st, s);
   const int ds_budget = st->sm_count - dvc;
   static const bool side_on = std::getenv("ATTN_BWD_NO_SIDE_STREAM") == nullptr;
-  if (side_on && dvc > 0 && ds_budget >= st->sm_count / 4) {
+  if (side_on && dvc > 0) {
     std::lock_guard<std::mutex> lk(st->side_mu);
     if (!st->side) {
       if (cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking) != cudaSuccess ||
@@ -391,14 +393,17 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
           cudaEventCreateWithFlags(&st->join, cudaEventDisableTiming) != cudaSuccess)
         return ATTN_BWD_ECUDA;
     }
+    const bool split = ds_budget >= st->sm_count / 4;
+    int rc_ds = ATTN_BWD_OK, rc_dv = ATTN_BWD_OK;
+    if (!split) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
     if (cudaEventRecord(st->fork, cs) != cudaSuccess || cudaStreamWaitEvent(st->side, st->fork, 0) != cudaSuccess)
       return ATTN_BWD_ECUDA;
-    const int rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
-    const int rc_ds = rc_dv ? ATTN_BWD_OK : launch_ds(*st, s, dO, P, V, M, p, dS, cs, ds_budget);
+    if (rc_ds == ATTN_BWD_OK) rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
+    if (split && rc_dv == ATTN_BWD_OK) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs, ds_budget);
     // join even after an error, so the caller's stream never runs ahead of issued work
     if (cudaEventRecord(st->join, st->side) != cudaSuccess || cudaStreamWaitEvent(cs, st->join, 0) != cudaSuccess)
       return ATTN_BWD_ECUDA;
-    return rc_dv ? rc_dv : rc_ds;
+    return rc_ds ? rc_ds : rc_dv;
   }
   rc = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
   if (rc) return rc;
