@@ -44,7 +44,7 @@ bool set_ds_smem() {
   (cudaFuncSetAttribute(ds::ds_kernel<R, M>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
                         ds::Cfg<R, M>::SMEM_BYTES) == cudaSuccess)
   return ATTN_BWD_SMEM(false, ds::kRecompute) && ATTN_BWD_SMEM(false, ds::kResident) &&
-         ATTN_BWD_SMEM(false, ds::kTmemP) && ATTN_BWD_SMEM(true, ds::kRecompute) &&
+         ATTN_BWD_SMEM(false, ds::kTmemP) && ATTN_BWD_SMEM(false, ds::kCompact) && ATTN_BWD_SMEM(true, ds::kRecompute) &&
          ATTN_BWD_SMEM(true, ds::kResident) && ATTN_BWD_SMEM(true, ds::kTmemP);
 #undef ATTN_BWD_SMEM
 }
@@ -119,11 +119,13 @@ int check_shape(const Shape& s) {
   return ATTN_BWD_OK;
 }
 
-// Pass-2 mode of the dS kernel, chosen per shape from B200 measurements:
+// Pass-2 mode of the dS kernel, chosen per shape from B200 measurements (clusters cost:
+// forcing c1 onto 2-CTA clusters made its dS kernel 27 % slower, so the modes that keep a
+// row in one CTA come first):
 //   ragged rows: kTmemP while a row fits 5 chunks per CTA on clusters of up to 8
 //     CTAs (its pass 2 avoids re-fetching unaligned rows: c2 dS 553 -> 348 us);
-//   aligned rows: kTmemP up to 4 chunks (no cluster), else kResident (6 shared
-//     P/mask stages beat 4 dedicated ones: c1 100 vs 120 us, c4 1886 vs 2138 us);
+//   aligned rows: kResident up to 8 chunks (6 shared P/mask stages beat kTmemP's 4
+//     dedicated ones: c1 100 vs 120 us), kCompact up to 10 chunks per CTA beyond that;
 //   then kResident on clusters up to 8 x 512 columns, then kRecompute.
 // ATTN_BWD_DS_MODE = 0/1/2 forces recompute / resident / TMEM-P where the shape
 // allows it (for measurements), read once.
@@ -191,15 +193,28 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
     prm.cpc = (prm.nchunks + prm.cs - 1) / prm.cs;
   };
   const int tp_max = ds::Cfg<false, ds::kTmemP>::NSLOT;
+  const int cp_max = ds::Cfg<false, ds::kCompact>::CP_MAX;
   const int forced = forced_ds_mode();
   int mode;
   const bool tp_pref = rag ? prm.nchunks <= 8 * tp_max : false;   // aligned rows: kResident measured faster
   if ((forced < 0 && tp_pref) || (forced == ds::kTmemP && prm.nchunks <= 8 * tp_max)) {
     mode = ds::kTmemP;
     split(tp_max);
+  } else if (!rag && prm.nchunks <= 8 * cp_max &&
+             ((forced < 0 && prm.nchunks > ds::TSLOTS) || forced == ds::kCompact)) {
+    // rows beyond 8 fp32 chunks: bf16 compact store first, clusters only beyond 10 chunks
+    mode = ds::kCompact;
+    split(cp_max);
   } else if (prm.nchunks <= 8 * ds::TSLOTS && forced != ds::kRecompute) {
     mode = ds::kResident;
     split(ds::TSLOTS);
+    // measurement knob: ATTN_BWD_DS_CLUSTER = n forces n CTAs per row (1..8) when it fits
+    static const int forced_cs = std::getenv("ATTN_BWD_DS_CLUSTER") ? std::atoi(std::getenv("ATTN_BWD_DS_CLUSTER")) : 0;
+    if (forced_cs >= 1 && forced_cs <= 8 && (prm.nchunks + forced_cs - 1) / forced_cs <= ds::TSLOTS &&
+        forced_cs <= prm.nchunks) {
+      prm.cs = forced_cs;
+      prm.cpc = (prm.nchunks + forced_cs - 1) / forced_cs;
+    }
   } else {
     mode = ds::kRecompute;
     prm.cs = 1;
@@ -228,6 +243,7 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   ATTN_BWD_PICK(false, ds::kRecompute)
   ATTN_BWD_PICK(false, ds::kResident)
   ATTN_BWD_PICK(false, ds::kTmemP)
+  ATTN_BWD_PICK(false, ds::kCompact)
   ATTN_BWD_PICK(true, ds::kRecompute)
   ATTN_BWD_PICK(true, ds::kResident)
   ATTN_BWD_PICK(true, ds::kTmemP)

@@ -58,21 +58,30 @@ constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 //   kTmemP      pass 1 writes the masked dP~ (fp32) and P (bf16 pairs) back into TMEM
 //               (96-column slots, <= 5 chunks per CTA), so pass 2 reads TMEM only and the
 //               whole shared-memory ring prefetches pass-1 data from HBM.
-enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2 };
+//   kCompact    MMAs land in a ring of 3 fp32 slots; pass 1 writes the masked dP~ back as
+//               bf16 pairs (32 columns per chunk) and frees the slot at once, so one CTA
+//               holds rows of up to 10 chunks (640 columns) without a cluster.  Pass 2
+//               re-reads P from L2.  Rounding dP~ to bf16 adds at most ~|P|·|dP~|·2^-9 to dS.
+enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2, kCompact = 3 };
 
 // Shared-memory plan per mode.  With dP~ resident the MMAs of a unit end with
 // pass 1, so one dO buffer suffices and the freed space buys P/mask stages
 // (bytes in flight are what keep HBM busy).
 template <bool RAG, int MODE>
 struct Cfg {
-  static constexpr bool RES = MODE != kRecompute;
+  static constexpr bool RES = MODE != kRecompute;     // each chunk's MMA is issued once
+  static constexpr bool HOLD = MODE == kResident || MODE == kTmemP;   // slots held until pass 2
+  static constexpr bool CP = MODE == kCompact;
+  static constexpr int CP_SLOTS = 3;                   // kCompact: fp32 ring slots
+  static constexpr int CP_BASE = CP_SLOTS * BN;        // kCompact: first column of the bf16 store
+  static constexpr int CP_MAX = (TSLOTS * BN - CP_BASE) / (BN / 2);   // kCompact: chunks per CTA (10)
   static constexpr bool TP = MODE == kTmemP;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
   static constexpr int VST = RAG ? 2 : RES ? (TP ? 2 : 2) : 3;
   static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
-  static constexpr int NSLOT = TP ? 5 : TSLOTS;        // TMEM slots (<= 512 columns)
+  static constexpr int NSLOT = TP ? 5 : CP ? CP_SLOTS : TSLOTS;   // TMEM slots (<= 512 columns)
   static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
   static constexpr int P_PITCH = RAG ? RAG_P_PITCH : 128;  // bytes per staged P row
   static constexpr int M_PITCH = RAG ? RAG_M_PITCH : 64;   // bytes per staged mask row
@@ -215,7 +224,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   using namespace sm100;
   using C = Cfg<RAG, MODE>;
   constexpr int PST = C::PST, VST = C::VST, DOBUF = C::DOBUF;
-  constexpr bool RES = C::RES, TP = C::TP;
+  constexpr bool RES = C::RES, TP = C::TP, HOLD = C::HOLD, CP = C::CP;
   constexpr int NSLOT = C::NSLOT, SLOTC = C::SLOTC;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -522,7 +531,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       uint32_t v[16];
       tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
       tmem_wait_ld();
-      if (!RES) {
+      if (!HOLD) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&T_empty[slot]);
@@ -568,6 +577,15 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         // P (bf16 pairs) in the slot's last 32 columns
         tmem_st16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
         tmem_st8(tmem_base + t_lane + slot * SLOTC + BN + cg * (CW / 2), pw);
+      }
+      if constexpr (CP) {
+        // masked dP~ as bf16 pairs into this chunk's 32 columns of the compact store
+        uint32_t tp[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          tp[k] = pack_bf16x2(__uint_as_float(v[2 * k] & mask_at(mx, 2 * k)),
+                              __uint_as_float(v[2 * k + 1] & mask_at(mx, 2 * k + 1)));
+        tmem_st8(tmem_base + t_lane + C::CP_BASE + cl * (BN / 2) + cg * (CW / 2), tp);
       }
       ++pi;
       return true;
@@ -638,21 +656,33 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         ++dsn;
         return true;
       } else {
-        int slot;
-        if (RES) {
-          slot = (job0 + cl) % NSLOT;
-        } else {
-          slot = job % NSLOT;
-          if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0304)) return false;
-          tc_fence_after();
-          ++job;
-        }
         uint32_t v[16];
-        tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&T_empty[slot]);
+        if constexpr (CP) {
+          // masked dP~ from the compact store, widened back to fp32 (mask already applied)
+          uint32_t tp[8];
+          tmem_ld8(tmem_base + t_lane + C::CP_BASE + cl * (BN / 2) + cg * (CW / 2), tp);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            v[2 * k] = tp[k] << 16;
+            v[2 * k + 1] = tp[k] & 0xFFFF0000u;
+          }
+        } else {
+          int slot;
+          if (RES) {
+            slot = (job0 + cl) % NSLOT;
+          } else {
+            slot = job % NSLOT;
+            if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0304)) return false;
+            tc_fence_after();
+            ++job;
+          }
+          tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&T_empty[slot]);
+        }
         const int ps = pi % PST;
         if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) return false;
         const unsigned long long el = row_el + (unsigned long long)c * BN;
@@ -697,7 +727,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         float acc0 = 0.f, acc1 = 0.f, r;
         for (int cl = 0; cl < nloc; ++cl)
           if (!p1_chunk(row_el, cl, acc0, acc1)) goto epi_done;
-        if (TP) tmem_wait_st();
+        if (TP || CP) tmem_wait_st();
         if (!exchange(acc0 + acc1, it, r)) goto epi_done;
         for (int cl = 0; cl < nloc; ++cl)
           if (!p2_chunk(bhl, mb, row_el, cl, job0, r)) goto epi_done;

@@ -188,9 +188,9 @@ print("BAD" if bad else "OK", bad)
 """
 
 
-@pytest.mark.parametrize("mode", ["0", "1", "2"])
+@pytest.mark.parametrize("mode", ["0", "1", "2", "3"])
 def test_every_ds_mode(mode, cuda):
-    """Each pass-2 mode of the dS kernel (recompute / resident / TMEM-held P), forced
+    """Each pass-2 mode of the dS kernel (recompute / resident / TMEM-held P / compact), forced
     through ATTN_BWD_DS_MODE where the shape allows it, aligned and ragged rows, with and
     without clusters, against the oracle (the variable is read once per process, hence
     the subprocess)."""
