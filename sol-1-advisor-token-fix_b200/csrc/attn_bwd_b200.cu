@@ -125,7 +125,8 @@ int check_shape(const Shape& s) {
 //   ragged rows: kTmemP while a row fits 5 chunks per CTA on clusters of up to 8
 //     CTAs (its pass 2 avoids re-fetching unaligned rows: c2 dS 553 -> 348 us);
 //   aligned rows: kResident up to 8 chunks (6 shared P/mask stages beat kTmemP's 4
-//     dedicated ones: c1 100 vs 120 us), kCompact up to 10 chunks per CTA beyond that;
+//     dedicated ones: c1 100 vs 120 us), kCompact for 9-10 chunks (one CTA instead of a
+//     cluster), kResident on clusters beyond that;
 //   then kResident on clusters up to 8 x 512 columns, then kRecompute.
 // ATTN_BWD_DS_MODE = 0/1/2 forces recompute / resident / TMEM-P where the shape
 // allows it (for measurements), read once.
@@ -200,9 +201,11 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   if ((forced < 0 && tp_pref) || (forced == ds::kTmemP && prm.nchunks <= 8 * tp_max)) {
     mode = ds::kTmemP;
     split(tp_max);
-  } else if (!rag && prm.nchunks <= 8 * cp_max &&
-             ((forced < 0 && prm.nchunks > ds::TSLOTS) || forced == ds::kCompact)) {
-    // rows beyond 8 fp32 chunks: bf16 compact store first, clusters only beyond 10 chunks
+  } else if (!rag && ((forced < 0 && prm.nchunks > ds::TSLOTS && prm.nchunks <= cp_max) ||
+                      (forced == ds::kCompact && prm.nchunks <= 8 * cp_max))) {
+    // 9-10 chunks: the bf16 compact store keeps the row in one CTA (c4 dS 1966 -> 1643 us);
+    // where a cluster is needed anyway, kResident's exact fp32 store measured faster
+    // (c3 1187 vs 1343 us), so kCompact is not used there
     mode = ds::kCompact;
     split(cp_max);
   } else if (prm.nchunks <= 8 * ds::TSLOTS && forced != ds::kRecompute) {
