@@ -34,6 +34,16 @@ struct DeviceState {
   int n_occ = 0;
   cudaEvent_t fork = nullptr, join = nullptr;
   std::mutex side_mu;   // one full call at a time uses the side stream
+  // Full calls replayed as CUDA graphs, keyed by their whole argument list (16-entry LRU).
+  struct GraphEntry {
+    uint64_t key[14];
+    int state;             // 0 empty, 1 seen once (ran eagerly), 2 graph ready
+    uint64_t last_use;
+    cudaGraphExec_t exec;
+  };
+  GraphEntry graphs[16] = {};
+  uint64_t graph_clock = 0;
+  cudaStream_t cap = nullptr;   // private stream the captures run on
 };
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
@@ -354,6 +364,115 @@ int prologue(DeviceState** st, const Shape& s) {
   return device_state(st);
 }
 
+
+// Issues the dS and dV kernels of one full call on stream cs (see attn_bwd_b200_shard).
+int enqueue_full_locked(DeviceState* st, const Shape& s, const void* dO, const void* P, const void* Pd, const void* V,
+                 const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs) {
+  int rc = ATTN_BWD_OK;
+  // The dS and dV kernels are independent (different inputs and outputs), so the dV
+  // kernel always runs on a side stream forked from the caller's stream, which waits for
+  // both at the end.  When dV needs fewer CTAs than SMs, the dS grid is sized to the
+  // remaining SMs and both run side by side (dV launched first); otherwise dS is launched
+  // first with the full grid and dV's CTAs take over SMs as dS CTAs finish, filling the
+  // dS kernel's tail.  ATTN_BWD_NO_SIDE_STREAM=1 runs them back to back on one stream.
+  const int dvc = dv_ctas(*st, s);
+  const int ds_budget = st->sm_count - dvc;
+  static const bool side_on = std::getenv("ATTN_BWD_NO_SIDE_STREAM") == nullptr;
+  if (side_on && dvc > 0) {
+        if (!st->side) {
+      if (cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking) != cudaSuccess ||
+          cudaEventCreateWithFlags(&st->fork, cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&st->join, cudaEventDisableTiming) != cudaSuccess)
+        return ATTN_BWD_ECUDA;
+    }
+    const bool split = ds_budget >= st->sm_count / 4;
+    int rc_ds = ATTN_BWD_OK, rc_dv = ATTN_BWD_OK;
+    if (!split) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
+    if (cudaEventRecord(st->fork, cs) != cudaSuccess || cudaStreamWaitEvent(st->side, st->fork, 0) != cudaSuccess)
+      return ATTN_BWD_ECUDA;
+    if (rc_ds == ATTN_BWD_OK) rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
+    if (split && rc_dv == ATTN_BWD_OK) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs, ds_budget);
+    // join even after an error, so the caller's stream never runs ahead of issued work
+    if (cudaEventRecord(st->join, st->side) != cudaSuccess || cudaStreamWaitEvent(cs, st->join, 0) != cudaSuccess)
+      return ATTN_BWD_ECUDA;
+    return rc_ds ? rc_ds : rc_dv;
+  }
+  rc = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
+  if (rc) return rc;
+  return launch_dv(*st, s, dO, Pd, dV, cs);
+}
+
+
+int enqueue_full(DeviceState* st, const Shape& s, const void* dO, const void* P, const void* Pd, const void* V,
+                 const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs) {
+  std::lock_guard<std::mutex> lk(st->side_mu);
+  return enqueue_full_locked(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
+}
+
+// A full call as a CUDA graph: the first sighting of an argument list runs eagerly, the
+// second captures the same launches (on a private stream, thread-local capture mode) into
+// a graph, later ones replay it with one cudaGraphLaunch on the caller's stream, which
+// removes most of the host-side launch cost for repeated calls on the same tensors.
+// The replay depends only on the argument list (pointers, shape, dropout, stream): input
+// contents may change freely between calls.  ATTN_BWD_NO_GRAPH=1 turns this off.
+int run_full(DeviceState* st, const Shape& s, const void* dO, const void* P, const void* Pd, const void* V,
+             const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs) {
+  static const bool graphs_on = std::getenv("ATTN_BWD_NO_GRAPH") == nullptr;
+  if (!graphs_on) return enqueue_full(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
+  // a caller that is itself capturing this stream gets the plain launches in its graph
+  cudaStreamCaptureStatus cap_status = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(cs, &cap_status) != cudaSuccess) return ATTN_BWD_ECUDA;
+  if (cap_status != cudaStreamCaptureStatusNone) return enqueue_full(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
+  uint32_t pbits;
+  std::memcpy(&pbits, &p, 4);
+  const uint64_t key[14] = {(uint64_t)dO, (uint64_t)P, (uint64_t)Pd, (uint64_t)V, (uint64_t)M, (uint64_t)dS,
+                            (uint64_t)dV, pbits, (uint64_t)s.bs, (uint64_t)s.sq, (uint64_t)s.skv, (uint64_t)s.u0,
+                            (uint64_t)s.u1, (uint64_t)cs};
+  std::lock_guard<std::mutex> lk(st->side_mu);
+  DeviceState::GraphEntry* hit = nullptr;
+  DeviceState::GraphEntry* victim = &st->graphs[0];
+  for (auto& g : st->graphs) {
+    if (g.state && std::memcmp(g.key, key, sizeof(key)) == 0) { hit = &g; break; }
+    if (!g.state || (victim->state && g.last_use < victim->last_use)) victim = &g;
+  }
+  const uint64_t now = ++st->graph_clock;
+  if (hit && hit->state == 2) {
+    hit->last_use = now;
+    return cudaGraphLaunch(hit->exec, cs) == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
+  }
+  if (!hit) {   // first sighting: remember it, run eagerly
+    if (victim->state == 2) cudaGraphExecDestroy(victim->exec);
+    std::memcpy(victim->key, key, sizeof(key));
+    victim->state = 1;
+    victim->last_use = now;
+    victim->exec = nullptr;
+    return enqueue_full_locked(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
+  }
+  // second sighting: capture, instantiate, launch
+  if (!st->cap && cudaStreamCreateWithFlags(&st->cap, cudaStreamNonBlocking) != cudaSuccess) return ATTN_BWD_ECUDA;
+  cudaGraph_t graph = nullptr;
+  if (cudaStreamBeginCapture(st->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return ATTN_BWD_ECUDA;
+  const int rc = enqueue_full_locked(st, s, dO, P, Pd, V, M, p, dS, dV, st->cap);
+  const cudaError_t ce = cudaStreamEndCapture(st->cap, &graph);
+  if (rc || ce != cudaSuccess || !graph) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    hit->state = 0;
+    return rc ? rc : ATTN_BWD_ECUDA;
+  }
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) {
+    hit->state = 0;
+    return ATTN_BWD_ECUDA;
+  }
+  hit->exec = exec;
+  hit->state = 2;
+  hit->last_use = now;
+  return cudaGraphLaunch(exec, cs) == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
+}
+
 }  // namespace
 
 extern "C" {
@@ -395,38 +514,7 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
       !aligned16(dV))
     return ATTN_BWD_EALIGN;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  // The dS and dV kernels are independent (different inputs and outputs), so the dV
-  // kernel always runs on a side stream forked from the caller's stream, which waits for
-  // both at the end.  When dV needs fewer CTAs than SMs, the dS grid is sized to the
-  // remaining SMs and both run side by side (dV launched first); otherwise dS is launched
-  // first with the full grid and dV's CTAs take over SMs as dS CTAs finish, filling the
-  // dS kernel's tail.  ATTN_BWD_NO_SIDE_STREAM=1 runs them back to back on one stream.
-  const int dvc = dv_ctas(*st, s);
-  const int ds_budget = st->sm_count - dvc;
-  static const bool side_on = std::getenv("ATTN_BWD_NO_SIDE_STREAM") == nullptr;
-  if (side_on && dvc > 0) {
-    std::lock_guard<std::mutex> lk(st->side_mu);
-    if (!st->side) {
-      if (cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking) != cudaSuccess ||
-          cudaEventCreateWithFlags(&st->fork, cudaEventDisableTiming) != cudaSuccess ||
-          cudaEventCreateWithFlags(&st->join, cudaEventDisableTiming) != cudaSuccess)
-        return ATTN_BWD_ECUDA;
-    }
-    const bool split = ds_budget >= st->sm_count / 4;
-    int rc_ds = ATTN_BWD_OK, rc_dv = ATTN_BWD_OK;
-    if (!split) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
-    if (cudaEventRecord(st->fork, cs) != cudaSuccess || cudaStreamWaitEvent(st->side, st->fork, 0) != cudaSuccess)
-      return ATTN_BWD_ECUDA;
-    if (rc_ds == ATTN_BWD_OK) rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
-    if (split && rc_dv == ATTN_BWD_OK) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs, ds_budget);
-    // join even after an error, so the caller's stream never runs ahead of issued work
-    if (cudaEventRecord(st->join, st->side) != cudaSuccess || cudaStreamWaitEvent(cs, st->join, 0) != cudaSuccess)
-      return ATTN_BWD_ECUDA;
-    return rc_ds ? rc_ds : rc_dv;
-  }
-  rc = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
-  if (rc) return rc;
-  return launch_dv(*st, s, dO, Pd, dV, cs);
+  return run_full(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
 }
 
 int attn_bwd_b200(const void* dO, const void* P, const void* Pd, const void* V, const uint8_t* M, float p, int bs,

@@ -204,3 +204,56 @@ def test_every_ds_mode(mode, cuda):
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip().startswith("OK"), r.stdout
+
+
+def test_replayed_calls_follow_input_contents(cuda):
+    """Repeated full calls on the same buffers are replayed from a cached launch graph; the
+    results must follow new input values written into those buffers, and must stay right
+    after more distinct argument lists than the cache holds have pushed the entry out."""
+    data = list(_to(generate_input(1, 96, 192, 40), cuda))
+    out = (torch.empty_like(data[1]), torch.empty_like(data[3]))
+    for seed in (41, 42, 43, 44):
+        new = generate_input(1, 96, 192, seed)
+        for i in range(5):
+            data[i].copy_(new[i])
+        ab.attn_bwd(tuple(data), out=out)
+        torch.cuda.synchronize()
+        rS, rV = attn_bwd_reference(new)
+        _close(f"dS seed {seed}", rS, out[0])
+        _close(f"dV seed {seed}", rV, out[1])
+    for skv in range(64, 64 + 24 * 16, 16):       # 24 other argument lists, each seen twice
+        small = _to(generate_input(1, 16, skv, 50), cuda)
+        ab.custom_kernel(small)
+        ab.custom_kernel(small)
+    new = generate_input(1, 96, 192, 45)
+    for i in range(5):
+        data[i].copy_(new[i])
+    ab.attn_bwd(tuple(data), out=out)
+    torch.cuda.synchronize()
+    assert ab.poll_error() == 0
+    rS, rV = attn_bwd_reference(new)
+    _close("dS after eviction", rS, out[0])
+    _close("dV after eviction", rV, out[1])
+
+
+def test_call_inside_caller_graph_capture(cuda):
+    """A full call captured into the caller's own CUDA graph replays correctly."""
+    data = _to(generate_input(1, 64, 128, 60), cuda)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            ab.custom_kernel(data)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        dS, dV = ab.custom_kernel(data)
+    new = generate_input(1, 64, 128, 61)
+    for i in range(5):
+        data[i].copy_(new[i].to(cuda))
+    g.replay()
+    torch.cuda.synchronize()
+    assert ab.poll_error() == 0
+    rS, rV = attn_bwd_reference(new)
+    _close("dS", rS, dS)
+    _close("dV", rV, dV)
