@@ -316,6 +316,16 @@ int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void*
     if (!make_map(&tm_Pd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, Pd, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return ATTN_BWD_ETMAP;
   }
+  // ragged rows: every 8th row is 16·skv bytes further, so rows of one class mod 8 form a
+  // 2-D tensor of 32-bit words (4·skv words per 8-row group) read as 8-row x 272 B boxes
+  const long long rows8 = rag ? (long long)nu * kGroups * s.sq / 8 : 0;
+  if (rows8 > 0) {
+    cuuint64_t dims[2] = {(cuuint64_t)s.skv * 4, (cuuint64_t)rows8};
+    cuuint64_t str[1] = {(cuuint64_t)s.skv * 16};
+    cuuint32_t box[2] = {dv::Cfg<true>::RAW_PITCH / 4, 8};
+    if (!make_map(&tm_Pd, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, Pd, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return ATTN_BWD_ETMAP;
+  }
   {
     cuuint64_t dims[4] = {kHeadDim, kHeads, (cuuint64_t)s.sq, (cuuint64_t)s.bs};
     cuuint64_t str[3] = {kHeadDim * 2, (cuuint64_t)kHeads * kHeadDim * 2, (cuuint64_t)s.sq * kHeads * kHeadDim * 2};
@@ -333,6 +343,7 @@ int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.err = st.err;
   prm.Pd = static_cast<const uint8_t*>(Pd);
   prm.pd_end16 = ((unsigned long long)nu * kGroups * s.sq * s.skv * 2 + 15) & ~15ull;
+  prm.tma_rows = rows8 * 8;
   const int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(dV);
   if (rag)

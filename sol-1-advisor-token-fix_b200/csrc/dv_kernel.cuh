@@ -17,12 +17,15 @@
 //
 // Row formats (template flag RAG):
 //   RAG = false  seq_kv % 8 == 0: P_drop tiles are TMA tensor tiles (128B swizzle).
-//   RAG = true   any seq_kv: P_drop rows are not 16-byte aligned; the producer
-//                fetches each 128-column row segment with an untiled bulk copy
-//                from the 16-byte boundary below it into a padded row (272 B),
-//                and warps 6..13 re-align the bytes in registers and write the
-//                128B-swizzled MN-major tile the MMA reads (zeroing columns >=
-//                seq_kv and rows >= seq_q).
+//   RAG = true   any seq_kv: P_drop rows are not 16-byte aligned.  Rows 8 apart are
+//                16·seq_kv bytes apart, a 16-byte multiple, so each residue class of
+//                rows mod 8 is a legal 2-D tensor: the producer fetches the 64 rows of
+//                a K chunk as 8 TMA boxes (one per class, 8 rows x 272 B from the
+//                16-byte boundary below each row's 128-column segment), and warps
+//                6..13 re-align the bytes in registers and write the 128B-swizzled
+//                MN-major tile the MMA reads (zeroing columns >= seq_kv and rows >=
+//                seq_q).  The last partial group of 8 rows of the buffer (outside
+//                the class tensor) is fetched by 16-byte cp.async instead.
 #pragma once
 #include "sm100.cuh"
 
@@ -36,10 +39,11 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
 template <bool RAG>
 struct Cfg {
-  static constexpr int kThreads = RAG ? 480 : 192;   // RAG: + 8 re-align warps (6..13) + 1 extra raw-row producer (14)
+  static constexpr int kThreads = RAG ? 448 : 192;    // RAG: + 8 re-align warps (6..13)
   static constexpr int ST = RAG ? 4 : 6;               // operand stages
   static constexpr int RST = RAG ? 4 : 0;              // raw P_drop row stages
-  static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack (raw_rows_async)
+  static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack
+  static constexpr int CLS_BYTES = 8 * RAW_PITCH;      // one class box: 8 rows (2176 B, 128-byte multiple)
   static constexpr int RAW_BYTES = BK * RAW_PITCH;
   static constexpr int OFF_RAW = ST * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_RAW + RST * RAW_BYTES;
@@ -58,6 +62,7 @@ struct Params {
   int* err;
   const uint8_t* Pd;              // local P_drop base (RAG path)
   unsigned long long pd_end16;    // bytes of P_drop rounded up to 16
+  long long tma_rows;             // RAG: rows covered by the class tensor map (8 · floor(rows / 8))
 };
 
 // out[j] = bytes [4j+sh, 4j+sh+4) of the little-endian stream `in` (NOUT+4 words).
@@ -73,30 +78,30 @@ __device__ __forceinline__ void byte_shift(const uint32_t* in, uint32_t sh, uint
   for (int j = 0; j < NOUT; ++j) out[j] = __funnelshift_r(v[j], v[j + 1], bits);
 }
 
-// Ragged P_drop rows: 16-byte cp.async of the 17 aligned words covering the
-// 128-column segment of rows [r_base, r_base+32) of a K chunk.  Lane = (row
-// offset lane/16, word lane%16; lane%16 == 0 also takes word 16), two rows per
-// step, the row start advanced by an add.  Words past the tensor's end (rounded
-// up to 16 bytes) are skipped; the re-align warps zero those columns.
-__device__ __forceinline__ void raw_rows_async(uint32_t rdst, const Params& prm, int bhl, int kc, int jt, int r_base,
-                                               uint32_t lane) {
-  constexpr int PITCH = 272;
-  const int w = int(lane & 15);
-  const int r0 = r_base + int(lane >> 4);
-  const int rows = min(32, prm.sq - kc * BK - r_base);
-  unsigned long long el = ((unsigned long long)bhl * prm.sq + kc * BK + r0) * prm.skv + (unsigned long long)jt * BM;
-  const unsigned long long step = 2ull * prm.skv;
-  for (int k = 0; 2 * k + int(lane >> 4) < rows; ++k, el += step) {
-    const int r = r0 + 2 * k;
+// Shared-memory row of logical row r (0..63) of a raw stage: class box r % 8, row r / 8.
+__device__ __forceinline__ int raw_row(int r) { return (r & 7) * 8 + (r >> 3); }
+
+// Fallback for K chunks that reach the buffer's last partial group of 8 rows: 16-byte
+// cp.async of the 17 aligned words covering each row's 128-column segment, into the
+// same layout the class boxes produce, then a wait for completion.  Words past the
+// tensor's end (rounded up to 16 bytes) are skipped; the re-align warps zero those
+// columns.
+__device__ __forceinline__ void raw_rows_sync(uint32_t rdst, const Params& prm, int bhl, int kc, int jt,
+                                              uint32_t lane) {
+  const int rows = min(BK, prm.sq - kc * BK);
+  for (int f = int(lane); f < rows * 17; f += 32) {
+    const int r = f / 17, w = f - r * 17;
+    const unsigned long long el = ((unsigned long long)bhl * prm.sq + kc * BK + r) * prm.skv + (unsigned long long)jt * BM;
     const unsigned long long src = ((el * 2) & ~15ull) + 16ull * w;
-    if (src < prm.pd_end16) sm100::cp_async16(rdst + r * PITCH + w * 16, prm.Pd + src);
-    if (w == 0 && src + 256 < prm.pd_end16) sm100::cp_async16(rdst + r * PITCH + 256, prm.Pd + src + 256);
+    if (src < prm.pd_end16) sm100::cp_async16(rdst + raw_row(r) * 272 + w * 16, prm.Pd + src);
   }
+  sm100::cp_async_wait_all();
 }
 
 template <bool RAG>
 __global__ void __launch_bounds__(Cfg<RAG>::kThreads, 1)
-dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  box (64,64,1) SW128
+dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_local) box (64,64,1) SW128;
+                                                       // RAG: u32 (4·skv, rows/8) box (68, 8), no swizzle
           const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)         box (64,1,64,1) SW128
           __nv_bfloat16* __restrict__ dV,              // local [units, skv, 128]
           const Params prm) {
@@ -120,14 +125,14 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
   const uint32_t warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 8); }
-    // raw_full: one cp.async completion arrive per lane of the two raw-row producer warps
-    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 64); mbar_init(&raw_empty[i], 8); }
+    // raw_full: the producer's lane 0 (with the class boxes' bytes as transaction count)
+    for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    if (!RAG) prefetch_tmap(&tm_Pd);
+    if (!RAG || prm.tma_rows > 0) prefetch_tmap(&tm_Pd);
     prefetch_tmap(&tm_dO);
   }
   if (warp == 1) { tmem_alloc(tmem_base_slot, 256); tmem_relinquish(); }
@@ -167,15 +172,28 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
           if constexpr (RAG) {
             const int rs = ri % RSTD;
             if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1102)) goto prod_done;
-            raw_rows_async(smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES), prm, bhl, kc, jt, 0, lane);
-            cp_async_arrive_noinc(&raw_full[rs]);
+            uint8_t* rdst = smem + C::OFF_RAW + rs * C::RAW_BYTES;
+            const long long r0 = (long long)bhl * prm.sq + kc * BK;
+            if (r0 + min(BK, prm.sq - kc * BK) <= prm.tma_rows) {
+              if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], C::RAW_BYTES);
+              __syncwarp();
+              if (lane < 8) {
+                // class box `lane`: rows r0 + lane + 8i, i < 8 (row k of its 8-row group)
+                const long long rm = r0 + lane;
+                const unsigned long long off = ((unsigned long long)(rm & 7) * 2 * prm.skv + (unsigned long long)jt * 256) & ~15ull;
+                tma_load_2d(rdst + lane * C::CLS_BYTES, &tm_Pd, &raw_full[rs], int(off >> 2), int(rm >> 3));
+              }
+            } else {
+              raw_rows_sync(smem_u32(rdst), prm, bhl, kc, jt, lane);
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&raw_full[rs]);
+            }
             ++ri;
           }
         }
       }
     }
   prod_done:
-    if (RAG) cp_async_wait_all();
     if (lane == 0) {
       for (uint32_t k = 0; k < uint32_t(ST) && k < si; ++k) {
         const uint32_t i = si - 1 - k;
@@ -260,30 +278,16 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
     }
   }
 
-  else if (RAG && warp == 14) {
-    // second raw-row producer: rows 32..63 of every K chunk (warp 0 does rows 0..31)
-    uint32_t ri = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const int ul = u / n_jt, jt = u - ul * n_jt;
-      for (int g = 0; g < kGroups; ++g) {
-        const int bhl = ul * kGroups + g;
-        for (int kc = 0; kc < n_kc; ++kc, ++ri) {
-          const int rs = ri % RSTD;
-          if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1103)) goto raw2_done;
-          raw_rows_async(smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES), prm, bhl, kc, jt, 32, lane);
-          cp_async_arrive_noinc(&raw_full[rs]);
-        }
-      }
-    }
-  raw2_done:
-    cp_async_wait_all();
-    __syncwarp();
-  }
   else if (RAG) {
-    // re-align warps 6..13: thread t handles row r = t % 64 of the chunk and the
-    // 32-column quarter qt = t / 64 (uniform per warp) of the 128-column tile
+    // re-align warps 6..13: thread t handles one row r of the chunk and the 32-column
+    // quarter qt = t / 64 (uniform per warp) of the 128-column tile.  Rows go diagonally
+    // over each group of 8 threads (i = t % 8, class m = (i + t/8) % 8, r = m + 8i), so
+    // both the raw-row reads (row 8m + i) and the swizzled writes (chunk ^ m) of a
+    // quarter-warp fall in 8 different 16-byte bank groups.
     const int t = int(threadIdx.x) - 6 * 32;
-    const int r = t & 63, qt = t >> 6;
+    const int qt = t >> 6;
+    const int ci = t & 7, cm = (ci + ((t >> 3) & 7)) & 7;
+    const int r = cm + 8 * ci;
     const int sq = prm.sq, skv = prm.skv;
     uint32_t si = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -299,7 +303,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // (skv, sq, bh_local)  b
           uint32_t w[16];
           if (srow < sq) {
             const unsigned long long el = ((unsigned long long)bhl * sq + srow) * skv + (unsigned long long)jt * BM;
-            const uint32_t src = smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES + r * C::RAW_PITCH + qt * 64);
+            const uint32_t src = smem_u32(smem + C::OFF_RAW + rs * C::RAW_BYTES + raw_row(r) * C::RAW_PITCH + qt * 64);
             uint32_t in[20];
 #pragma unroll
             for (int i = 0; i < 5; ++i) {
