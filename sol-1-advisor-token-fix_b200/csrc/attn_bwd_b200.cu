@@ -95,13 +95,55 @@ int device_state(DeviceState** out) {
   return st.rc;
 }
 
-bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
-              const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = g_encode(m, dt, rank, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// Encoded descriptors, direct-mapped by a hash of every encode argument (a descriptor
+// depends on nothing else), so repeated calls on the same tensors skip the driver call.
+// ATTN_BWD_NO_MAP_CACHE=1 encodes every time.
+struct MapEntry {
+  uint64_t key[16];
+  bool valid;
+  CUtensorMap map;
+};
+constexpr int kMapCacheSize = 256;
+MapEntry g_maps[kMapCacheSize];
+std::mutex g_map_mu;
+
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+              const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+  static const bool cache_on = std::getenv("ATTN_BWD_NO_MAP_CACHE") == nullptr;
+  if (!cache_on || rank > 5) return encode_map(m, dt, rank, ptr, dims, strides, box, sw);
+  uint64_t key[16] = {};
+  key[0] = (uint64_t)dt | ((uint64_t)rank << 8) | ((uint64_t)sw << 16);
+  key[1] = (uint64_t)reinterpret_cast<uintptr_t>(ptr);
+  for (int i = 0; i < rank; ++i) {
+    key[2 + i] = dims[i];
+    key[7 + i] = box[i];
+    if (i + 1 < rank) key[12 + i] = strides[i];
+  }
+  uint64_t h = 1469598103934665603ull;   // FNV-1a over the key words
+  for (uint64_t w : key) h = (h ^ w) * 1099511628211ull;
+  MapEntry& e = g_maps[h % kMapCacheSize];
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    if (e.valid && std::memcmp(e.key, key, sizeof(key)) == 0) {
+      *m = e.map;
+      return true;
+    }
+  }
+  if (!encode_map(m, dt, rank, ptr, dims, strides, box, sw)) return false;
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  std::memcpy(e.key, key, sizeof(key));
+  e.map = *m;
+  e.valid = true;
+  return true;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -298,7 +340,7 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
 }
 
 int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void* Pd, void* dV,
-              cudaStream_t stream) {
+              cudaStream_t stream, int max_ctas = 0) {
   const int nu = s.n_units();
   if (nu == 0 || s.skv == 0) return ATTN_BWD_OK;
   if (s.sq == 0) {  // empty sum over seq_q: dV = 0
@@ -344,7 +386,8 @@ int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.Pd = static_cast<const uint8_t*>(Pd);
   prm.pd_end16 = ((unsigned long long)nu * kGroups * s.sq * s.skv * 2 + 15) & ~15ull;
   prm.tma_rows = rows8 * 8;
-  const int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
+  int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
+  if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(dV);
   if (rag)
     dv::dv_kernel<true><<<grid, dv::Cfg<true>::kThreads, dv::Cfg<true>::SMEM_BYTES, stream>>>(tm_Pd, tm_dO, out, prm);
@@ -382,27 +425,48 @@ int enqueue_full_locked(DeviceState* st, const Shape& s, const void* dO, const v
   int rc = ATTN_BWD_OK;
   // The dS and dV kernels are independent (different inputs and outputs), so the dV
   // kernel always runs on a side stream forked from the caller's stream, which waits for
-  // both at the end.  When dV needs fewer CTAs than SMs, the dS grid is sized to the
-  // remaining SMs and both run side by side (dV launched first); otherwise dS is launched
-  // first with the full grid and dV's CTAs take over SMs as dS CTAs finish, filling the
-  // dS kernel's tail.  ATTN_BWD_NO_SIDE_STREAM=1 runs them back to back on one stream.
+  // both at the end.  Two forms, chosen from B200 measurements over the SOL-ExecBench
+  // shapes and the benchmark configs:
+  //   split  (up to 256M score elements; ragged rows: 64M): dV is launched first on a
+  //          fixed share of the SMs (32 of 148; ragged rows 48) and runs persistently
+  //          next to a dS grid sized to the rest.  Both kernels are latency-bound at
+  //          these sizes and overlap well (64x128x128: 178 -> 143 us, 8x128x128:
+  //          37 -> 31 us);
+  //   plain  (larger): dS is launched first with the full grid and dV's CTAs take over
+  //          SMs as dS CTAs finish, filling the dS kernel's tail (1x4096x4096: 2306 us
+  //          back to back -> 1979 us).
+  // ATTN_BWD_NO_SIDE_STREAM=1 runs them back to back on one stream.
   const int dvc = dv_ctas(*st, s);
-  const int ds_budget = st->sm_count - dvc;
+  const bool rag_rows = !tma_rows_ok(s.skv);
+  const double elems = (double)s.n_units() * kGroups * s.sq * s.skv;
+  const bool small = elems <= (rag_rows ? 64e6 : 256e6);
+  const int dv_share = (st->sm_count * (rag_rows ? 48 : 32) + 147) / 148;
   static const bool side_on = std::getenv("ATTN_BWD_NO_SIDE_STREAM") == nullptr;
   if (side_on && dvc > 0) {
-        if (!st->side) {
+    if (!st->side) {
       if (cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking) != cudaSuccess ||
           cudaEventCreateWithFlags(&st->fork, cudaEventDisableTiming) != cudaSuccess ||
           cudaEventCreateWithFlags(&st->join, cudaEventDisableTiming) != cudaSuccess)
         return ATTN_BWD_ECUDA;
     }
-    const bool split = ds_budget >= st->sm_count / 4;
+    // measurement knobs: ATTN_BWD_SPLIT=0/1 forces the plain / split form, ATTN_BWD_DV_SMS=n
+    // sets the dV share of the split form
+    static const int force_split = std::getenv("ATTN_BWD_SPLIT") ? std::atoi(std::getenv("ATTN_BWD_SPLIT")) : -1;
+    static const int dv_sms = std::getenv("ATTN_BWD_DV_SMS") ? std::atoi(std::getenv("ATTN_BWD_DV_SMS")) : 0;
+    int dv_grid = dv_sms > 0 ? dv_sms : dv_share;
+    if (dv_grid > dvc) dv_grid = dvc;
+    const int budget = st->sm_count - dv_grid;
+    const bool split = budget > 0 && (force_split >= 0 ? force_split == 1 : small);
     int rc_ds = ATTN_BWD_OK, rc_dv = ATTN_BWD_OK;
-    if (!split) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
     if (cudaEventRecord(st->fork, cs) != cudaSuccess || cudaStreamWaitEvent(st->side, st->fork, 0) != cudaSuccess)
       return ATTN_BWD_ECUDA;
-    if (rc_ds == ATTN_BWD_OK) rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
-    if (split && rc_dv == ATTN_BWD_OK) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs, ds_budget);
+    if (split) {
+      rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side, dv_grid);
+      if (rc_dv == ATTN_BWD_OK) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs, budget);
+    } else {
+      rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
+      if (rc_ds == ATTN_BWD_OK) rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
+    }
     // join even after an error, so the caller's stream never runs ahead of issued work
     if (cudaEventRecord(st->join, st->side) != cudaSuccess || cudaStreamWaitEvent(cs, st->join, 0) != cudaSuccess)
       return ATTN_BWD_ECUDA;
