@@ -153,10 +153,36 @@ def _stream_handle(device_index):
     return torch.cuda.current_stream(device_index).cuda_stream
 
 
+def _load_torch_fast():
+    """The C++ host binding (csrc/torch_fast.cpp), or None when it is not built or when
+    ATTN_BWD_B200_LIB selects another build of the library (the binding links the
+    in-tree one)."""
+    import os
+    if os.environ.get("ATTN_BWD_B200_LIB") or os.environ.get("ATTN_BWD_NO_TORCH_BINDING"):
+        return None
+    try:
+        from . import _torch_fast
+    except ImportError:
+        return None
+    return _torch_fast.fast
+
+
+_torch_fast_fn = _load_torch_fast()
+
+
 def attn_bwd(data, out=None):
     """Full call; returns fresh (dS [bs,80,sq,skv], dV [bs,8,skv,128]) bf16 tensors
     unless ``out`` supplies preallocated ones."""
     dO, P, Pd, V, M, p = data
+    if out is None and _torch_fast_fn is not None and isinstance(dO, torch.Tensor):
+        try:
+            r = _torch_fast_fn(dO, P, Pd, V, M, float(p))
+        except TypeError:   # not tensors: the general path reports it
+            r = None
+        if r is not None:
+            if isinstance(r, int):
+                raise AttnBwdError("attn_bwd_b200", r)
+            return r
     if out is None and _fast_ok(dO, P, Pd, V, M):
         idx = dO.device.index
         if idx != torch.cuda.current_device():

@@ -58,3 +58,16 @@ def test_bad_unit_range_rejected_without_device():
     assert rc == _lib.EINVAL
     rc = lib.attn_bwd_b200_dv_shard(nul, nul, 2, 4, 16, 5, 4, nul, nul)
     assert rc == _lib.EINVAL
+
+
+def test_torch_binding_loads_and_declines_cpu_tensors():
+    """The C++ host binding is built in-tree, links the same library, and hands inputs
+    it cannot take (here: CPU tensors) back to the general path instead of computing."""
+    import torch
+    import attn_bwd_b200 as ab
+    assert ab._torch_fast_fn is not None
+    dO = torch.zeros(1, 4, 80, 128, dtype=torch.bfloat16)
+    P = torch.zeros(1, 80, 4, 8, dtype=torch.bfloat16)
+    V = torch.zeros(1, 8, 8, 128, dtype=torch.bfloat16)
+    M = torch.zeros(1, 80, 4, 8, dtype=torch.bool)
+    assert ab._torch_fast_fn(dO, P, P, V, M, 0.1) is None
