@@ -543,8 +543,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       uint32_t pw[8], mw[4], mx[4];
       load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row,
                     cg, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&PM_empty[ps]);
       expand_mask(mw, use_mask, mx);
       const int nvalid = RAG ? min(max(skv - (c * BN + cg * CW), 0), CW) : CW;
       if (RAG && nvalid < CW) {
@@ -572,6 +570,10 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           v[2 * k + 1] &= m1;
         }
       }
+      // the stage goes back to the producer only after every lane has consumed what it
+      // read from it (a release right after the loads let the next fill race them)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&PM_empty[ps]);
       if constexpr (TP) {
         // keep what pass 2 needs in TMEM: masked dP~ over the accumulator columns,
         // P (bf16 pairs) in the slot's last 32 columns
