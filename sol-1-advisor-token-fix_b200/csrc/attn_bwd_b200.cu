@@ -53,9 +53,12 @@ bool set_ds_smem() {
 #define ATTN_BWD_SMEM(R, M)                                                                               \
   (cudaFuncSetAttribute(ds::ds_kernel<R, M>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
                         ds::Cfg<R, M>::SMEM_BYTES) == cudaSuccess)
-  return ATTN_BWD_SMEM(false, ds::kRecompute) && ATTN_BWD_SMEM(false, ds::kResident) &&
-         ATTN_BWD_SMEM(false, ds::kTmemP) && ATTN_BWD_SMEM(false, ds::kCompact) && ATTN_BWD_SMEM(true, ds::kRecompute) &&
-         ATTN_BWD_SMEM(true, ds::kResident) && ATTN_BWD_SMEM(true, ds::kTmemP);
+  return ATTN_BWD_SMEM(ds::kRowsAligned, ds::kRecompute) && ATTN_BWD_SMEM(ds::kRowsAligned, ds::kResident) &&
+         ATTN_BWD_SMEM(ds::kRowsAligned, ds::kTmemP) && ATTN_BWD_SMEM(ds::kRowsAligned, ds::kCompact) &&
+         ATTN_BWD_SMEM(ds::kRowsRagged, ds::kRecompute) && ATTN_BWD_SMEM(ds::kRowsRagged, ds::kResident) &&
+         ATTN_BWD_SMEM(ds::kRowsRagged, ds::kTmemP) && ATTN_BWD_SMEM(ds::kRowsClass, ds::kRecompute) &&
+         ATTN_BWD_SMEM(ds::kRowsClass, ds::kResident) && ATTN_BWD_SMEM(ds::kRowsClass, ds::kTmemP) &&
+         ATTN_BWD_SMEM(ds::kRowsClass, ds::kCompact);
 #undef ATTN_BWD_SMEM
 }
 
@@ -204,7 +207,23 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
               const uint8_t* M, float p, void* dS, cudaStream_t stream, int max_ctas = 0) {
   const int nbh = s.n_units() * kGroups;
   if (nbh == 0 || s.sq == 0 || s.skv == 0) return ATTN_BWD_OK;
+  // Rows whose length is not a multiple of 16 bytes: class tiles (16·64 rows per tile set)
+  // when they waste fewer row slots than 128-row blocks per head do, else the per-row
+  // re-aligning kernel.  Measured on B200 (dS us, class / per-row): c2 296 / 339,
+  // 32x691x773 2720 / 3730, 8x373x449 249 / 240, 4x211x293 88 / 62.
+  // ATTN_BWD_RAGGED_ROWS=1 / ATTN_BWD_CLASS_ROWS=1 force one of the two.
+  static const bool force_ragged = std::getenv("ATTN_BWD_RAGGED_ROWS") != nullptr;
+  static const bool force_class = std::getenv("ATTN_BWD_CLASS_ROWS") != nullptr;
   const bool rag = !tma_rows_ok(s.skv);
+  int rk = ds::kRowsAligned;
+  if (rag) {
+    const long long per_class = (kGroups * (long long)s.sq + 15) / 16;
+    const long long class_slots = (per_class + 63) / 64 * 64 * 16;
+    const long long block_slots = (long long)kGroups * ((s.sq + ds::BM - 1) / ds::BM) * ds::BM;
+    rk = (force_class || (!force_ragged && class_slots < block_slots)) ? ds::kRowsClass : ds::kRowsRagged;
+  }
+  const long long total_rows = (long long)nbh * s.sq;
+  const long long cls_y = rk == ds::kRowsClass ? total_rows / 16 : 0;
   CUtensorMap tm_dO, tm_V, tm_P, tm_M, tm_dS;
   std::memset(&tm_P, 0, sizeof(tm_P));
   std::memset(&tm_M, 0, sizeof(tm_M));
@@ -233,27 +252,54 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
         !make_map(&tm_M, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, M, dims, str1, box, CU_TENSOR_MAP_SWIZZLE_64B))
       return ATTN_BWD_ETMAP;
   }
+  if (cls_y > 0) {
+    // class rows: the local P / mask buffers as 16-row groups, 16·skv elements each; a box
+    // is 64 rows of one class (64 groups) x one 64-column window
+    cuuint64_t dims[2] = {(cuuint64_t)s.skv * 16, (cuuint64_t)cls_y};
+    cuuint64_t str2[1] = {(cuuint64_t)s.skv * 32};
+    cuuint64_t str1[1] = {(cuuint64_t)s.skv * 16};
+    cuuint32_t boxp[2] = {ds::BN, 64};
+    cuuint32_t boxm[2] = {ds::CLS_M_PITCH, 64};
+    if (!make_map(&tm_P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, P, dims, str2, boxp, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_dS, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dS, dims, str2, boxp, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tm_M, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, M, dims, str1, boxm, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return ATTN_BWD_ETMAP;
+  }
   ds::Params prm;
   prm.sq = s.sq;
   prm.skv = s.skv;
-  prm.n_mb = (s.sq + ds::BM - 1) / ds::BM;
-  prm.n_units = nbh * prm.n_mb;
-  prm.nchunks = (s.skv + ds::BN - 1) / ds::BN;
+  if (rk == ds::kRowsClass) {
+    // units: (kv group, class pair, 64-row tile); a window starts up to 7 columns early
+    const int per_class = (kGroups * s.sq + 15) / 16;
+    prm.cls_T = (per_class + 63) / 64;
+    prm.cls_Y = (int)cls_y;
+    prm.n_mb = 1;
+    prm.n_units = s.n_units() * 8 * prm.cls_T;
+    prm.nchunks = (s.skv + 7 + ds::BN - 1) / ds::BN;
+  } else {
+    prm.cls_T = 1;
+    prm.cls_Y = 0;
+    prm.n_mb = (s.sq + ds::BM - 1) / ds::BM;
+    prm.n_units = nbh * prm.n_mb;
+    prm.nchunks = (s.skv + ds::BN - 1) / ds::BN;
+  }
+  prm.dO = static_cast<const uint8_t*>(dO);
   // Rows that do not fit one CTA's TMEM plan are split over a cluster of cs <= 8
   // CTAs (CTA k owns chunks [k*cpc, (k+1)*cpc)); the CTAs exchange row sums.
   auto split = [&](int per_cta) {
     prm.cs = (prm.nchunks + per_cta - 1) / per_cta;
     prm.cpc = (prm.nchunks + prm.cs - 1) / prm.cs;
   };
-  const int tp_max = ds::Cfg<false, ds::kTmemP>::NSLOT;
-  const int cp_max = ds::Cfg<false, ds::kCompact>::CP_MAX;
+  const int tp_max = ds::Cfg<ds::kRowsAligned, ds::kTmemP>::NSLOT;
+  const int cp_max = ds::Cfg<ds::kRowsAligned, ds::kCompact>::CP_MAX;
   const int forced = forced_ds_mode();
   int mode;
-  const bool tp_pref = rag ? prm.nchunks <= 8 * tp_max : false;   // aligned rows: kResident measured faster
+  // per-row re-aligned rows: kTmemP; aligned and class rows: kResident measured faster
+  const bool tp_pref = rk == ds::kRowsRagged ? prm.nchunks <= 8 * tp_max : false;
   if ((forced < 0 && tp_pref) || (forced == ds::kTmemP && prm.nchunks <= 8 * tp_max)) {
     mode = ds::kTmemP;
     split(tp_max);
-  } else if (!rag && ((forced < 0 && prm.nchunks > ds::TSLOTS && prm.nchunks <= cp_max) ||
+  } else if (rk != ds::kRowsRagged && ((forced < 0 && prm.nchunks > ds::TSLOTS && prm.nchunks <= cp_max) ||
                       (forced == ds::kCompact && prm.nchunks <= 8 * cp_max))) {
     // 9-10 chunks: the bf16 compact store keeps the row in one CTA (c4 dS 1966 -> 1643 us);
     // where a cluster is needed anyway, kResident's exact fp32 store measured faster
@@ -291,17 +337,21 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
                const ds::Params) = nullptr;
   int smem = 0;
 #define ATTN_BWD_PICK(R, M)                    \
-  if (rag == R && mode == M) {                 \
+  if (rk == R && mode == M) {                  \
     kern = ds::ds_kernel<R, M>;                \
     smem = ds::Cfg<R, M>::SMEM_BYTES;          \
   }
-  ATTN_BWD_PICK(false, ds::kRecompute)
-  ATTN_BWD_PICK(false, ds::kResident)
-  ATTN_BWD_PICK(false, ds::kTmemP)
-  ATTN_BWD_PICK(false, ds::kCompact)
-  ATTN_BWD_PICK(true, ds::kRecompute)
-  ATTN_BWD_PICK(true, ds::kResident)
-  ATTN_BWD_PICK(true, ds::kTmemP)
+  ATTN_BWD_PICK(ds::kRowsAligned, ds::kRecompute)
+  ATTN_BWD_PICK(ds::kRowsAligned, ds::kResident)
+  ATTN_BWD_PICK(ds::kRowsAligned, ds::kTmemP)
+  ATTN_BWD_PICK(ds::kRowsAligned, ds::kCompact)
+  ATTN_BWD_PICK(ds::kRowsRagged, ds::kRecompute)
+  ATTN_BWD_PICK(ds::kRowsRagged, ds::kResident)
+  ATTN_BWD_PICK(ds::kRowsRagged, ds::kTmemP)
+  ATTN_BWD_PICK(ds::kRowsClass, ds::kRecompute)
+  ATTN_BWD_PICK(ds::kRowsClass, ds::kResident)
+  ATTN_BWD_PICK(ds::kRowsClass, ds::kTmemP)
+  ATTN_BWD_PICK(ds::kRowsClass, ds::kCompact)
 #undef ATTN_BWD_PICK
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

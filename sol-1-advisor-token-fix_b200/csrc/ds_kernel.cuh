@@ -24,15 +24,30 @@
 //   warps 4..19  epilogue; warp w reads TMEM lanes 32·(w%4).. and chunk
 //                columns 16·((w-4)/4) ..+16
 //
-// Two row formats (template flag RAG):
-//   RAG = false  seq_kv % 16 == 0: P / mask chunks are TMA tensor tiles
-//                (128B / 64B swizzle) and dS leaves by TMA tensor store.
-//   RAG = true   any seq_kv: rows of P / mask are not 16-byte aligned, so each
-//                row segment is fetched by its own untiled bulk copy from the
-//                16-byte boundary below it into a padded row (pitch 144 B / 80 B);
-//                the epilogue re-aligns it in registers (funnel shifts), masks
-//                columns >= seq_kv, and stores dS through a per-warp transpose
-//                buffer with coalesced 2-byte stores.
+// Three row formats (template parameter RK):
+//   kRowsAligned  seq_kv % 16 == 0: P / mask chunks are TMA tensor tiles
+//                 (128B / 64B swizzle) and dS leaves by TMA tensor store.
+//   kRowsRagged   any seq_kv: rows of P / mask are not 16-byte aligned, so each
+//                 row segment is fetched by 16-byte cp.async from the 16-byte
+//                 boundary below it into a padded row (pitch 144 B / 80 B); the
+//                 epilogue re-aligns it in registers (funnel shifts), masks
+//                 columns >= seq_kv, and stores dS through a per-warp transpose
+//                 buffer with coalesced 2-byte stores.
+//   kRowsClass    any seq_kv, rows grouped by alignment class.  Row R of the
+//                 flat P buffer starts at element R·seq_kv, so its misalignment
+//                 depends only on R mod 16, and rows 16 apart are 32·seq_kv
+//                 bytes apart (a 16-byte multiple).  The 10 query heads of one
+//                 (batch, kv-head) share V and are contiguous in P, so a unit is
+//                 64 rows of class k plus 64 rows of class k+8 (k < 8) of one
+//                 kv group: both share the P misalignment s = k·seq_kv mod 8.
+//                 The MMA's V window is shifted to start at column -s, which
+//                 makes every P / dS word of the tile 16-byte aligned: P and the
+//                 mask arrive as per-class TMA boxes (2 each per chunk) in the
+//                 aligned layouts, dO rows are gathered by cp.async, the
+//                 epilogue is the aligned one (plus column bounds in the first
+//                 and last chunk), and dS leaves by TMA store through a dS class
+//                 map, except in a row's first and last chunk, where warp 3
+//                 writes it with 16-byte stores.
 #pragma once
 #include "sm100.cuh"
 
@@ -63,12 +78,16 @@ constexpr int V_BYTES = BN * kHeadDim * 2;    // 16 KB
 //               holds rows of up to 10 chunks (640 columns) without a cluster.  Pass 2
 //               re-reads P from L2.  Rounding dP~ to bf16 adds at most ~|P|·|dP~|·2^-9 to dS.
 enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2, kCompact = 3 };
+enum RowKind : int { kRowsAligned = 0, kRowsRagged = 1, kRowsClass = 2 };
+constexpr int CLS_M_PITCH = 80;   // class rows: 64 B of mask row + 16 B (window may start 8 B into a word)
 
 // Shared-memory plan per mode.  With dP~ resident the MMAs of a unit end with
 // pass 1, so one dO buffer suffices and the freed space buys P/mask stages
 // (bytes in flight are what keep HBM busy).
-template <bool RAG, int MODE>
+template <int RK, int MODE>
 struct Cfg {
+  static constexpr bool RAG = RK == kRowsRagged;
+  static constexpr bool CLS = RK == kRowsClass;
   static constexpr bool RES = MODE != kRecompute;     // each chunk's MMA is issued once
   static constexpr bool HOLD = MODE == kResident || MODE == kTmemP;   // slots held until pass 2
   static constexpr bool CP = MODE == kCompact;
@@ -79,12 +98,12 @@ struct Cfg {
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
   static constexpr int VST = RAG ? 2 : RES ? (TP ? 2 : 2) : 3;
-  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : (RES ? 6 : 4);
+  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : CLS ? (RES ? 5 : 3) : (RES ? 6 : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
   static constexpr int NSLOT = TP ? 5 : CP ? CP_SLOTS : TSLOTS;   // TMEM slots (<= 512 columns)
   static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
   static constexpr int P_PITCH = RAG ? RAG_P_PITCH : 128;  // bytes per staged P row
-  static constexpr int M_PITCH = RAG ? RAG_M_PITCH : 64;   // bytes per staged mask row
+  static constexpr int M_PITCH = RAG ? RAG_M_PITCH : CLS ? CLS_M_PITCH : 64;   // bytes per staged mask row
   static constexpr int P_BYTES = BM * P_PITCH;
   static constexpr int M_BYTES = BM * M_PITCH;
   static constexpr int STG_PITCH = 48;                 // per-warp dS transpose rows (RAG): 32 B + pad
@@ -102,7 +121,8 @@ struct Cfg {
   static constexpr int OFF_RX = OFF_BAR + NBAR * 8;    // float rx[2][4][128]: per-column-group row sums
   static constexpr int OFF_XB = OFF_RX + 2 * 4 * BM * 4;   // float xb[2][8][128]: row sums from each cluster CTA
   static constexpr int OFF_MISC = OFF_XB + 2 * 8 * BM * 4;   // tmem base, abort flag, cluster exchange barrier
-  static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+  static constexpr int OFF_DOTAB = OFF_MISC + 64;             // class rows: byte offsets of the tile's 128 dO rows
+  static constexpr int SMEM_BYTES = OFF_DOTAB + (CLS ? BM * 8 : 0) + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "dS kernel shared memory");
 };
 
@@ -124,7 +144,60 @@ struct Params {
   uint8_t* dS;
   unsigned long long p_end16;   // bytes of P rounded up to 16 (bulk copies never read past it)
   unsigned long long m_end16;   // same for the mask
+  // kRowsClass
+  const uint8_t* dO;            // dO base ([bs, sq, 80, 128]); rows are gathered by cp.async
+  int cls_T;                    // 64-row tiles per class per kv group
+  int cls_Y;                    // 16-row groups of the local P buffer the class tensor maps cover
 };
+
+// kRowsClass unit u = (local kv group ul, tile t, class pair k), k fastest.
+struct ClsUnit {
+  long long g0;     // local flat row of the group's first row (ul · 10 · sq)
+  int rho[2];       // group row of tile row 0 of sub-class A (class k) / B (class k+8); rows step 16
+  int cls[2];       // the two classes (R mod 16)
+  int s;            // P misalignment of the tile's rows in elements: chunk c covers columns 64c-s ..
+  int mo[2];        // byte offset (0 or 8) of each sub-class's mask window inside its 16-byte word
+  int zv;           // V index b·8 + kv-head
+  int ug;           // global (batch, kv-head) index
+  bool fallback;    // a row lies past the class maps' extent: fetch by cp.async
+  bool pad;         // a sub-class has fewer than 64 rows: the tile holds padding rows
+};
+
+__device__ __forceinline__ ClsUnit cls_unit(int u, const Params& prm) {
+  ClsUnit x;
+  const int T = prm.cls_T;
+  // the 8 class pairs of one row range are consecutive units, so neighbouring CTAs read
+  // the 16 classes of the same 16-row groups at the same time (DRAM page locality)
+  const int k = u & 7;
+  const int t = (u >> 3) % T;
+  const int ul = u / (8 * T);
+  const int rows = kGroups * prm.sq;
+  x.g0 = (long long)ul * rows;
+  x.s = (k * prm.skv) & 7;
+  x.fallback = false;
+  x.pad = false;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int cl = k + 8 * h;
+    x.cls[h] = cl;
+    const int r0 = int(((long long)cl - x.g0) & 15);   // first group row of this class
+    const int n = r0 < rows ? (rows - 1 - r0) / 16 + 1 : 0;   // rows of this class in the group
+    // tile t covers class rows [64t, 64t+64); the last tile is moved back to end at row n,
+    // overlapping its predecessor (rows computed twice get bit-identical values), so only
+    // classes with fewer than 64 rows leave padding rows in a tile
+    const int b0 = min(64 * t, max(n - 64, 0));
+    if (n < 64) x.pad = true;
+    x.rho[h] = r0 + 16 * b0;
+    x.mo[h] = int(((long long)cl * prm.skv - x.s) & 15);
+    if (x.rho[h] < rows) {
+      const int last = min(x.rho[h] + 16 * 63, x.rho[h] + 16 * ((rows - 1 - x.rho[h]) / 16));
+      if ((x.g0 + last) / 16 >= prm.cls_Y) x.fallback = true;
+    }
+  }
+  x.ug = prm.bh_base / kGroups + ul;
+  x.zv = x.ug;
+  return x;
+}
 
 // Shifts a little-endian byte stream right by `sh` bytes (0..15):
 // out[j] = bytes [4j+sh, 4j+sh+4) of `in`.  `in` holds NOUT+4 words.
@@ -186,6 +259,29 @@ __device__ __forceinline__ uint32_t mask_at(const uint32_t (&mx)[4], int e) {
   return __byte_perm(mx[e >> 2], 0u, (e & 3) * 0x1111u);
 }
 
+// kRowsClass: P as in the aligned layout (128B swizzle); mask rows at pitch 80 with the
+// window starting `mo` (0 or 8, uniform per warp) bytes into the row.
+__device__ __forceinline__ void load_row_cls(uint32_t p_stage, uint32_t m_stage, int row, int cg, int mo,
+                                             uint32_t (&pw)[8], uint32_t (&mw)[4]) {
+  using namespace sm100;
+  const uint32_t p_row = p_stage + row * 128;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint4 t = lds128(p_row + (((cg * 2 + i) ^ (row & 7)) << 4));
+    pw[4 * i] = t.x; pw[4 * i + 1] = t.y; pw[4 * i + 2] = t.z; pw[4 * i + 3] = t.w;
+  }
+  const uint32_t m_addr = m_stage + row * CLS_M_PITCH + cg * 16;
+  if (mo == 0) {
+    const uint4 t = lds128(m_addr);
+    mw[0] = t.x; mw[1] = t.y; mw[2] = t.z; mw[3] = t.w;
+  } else {
+    uint32_t a, b, c2, d;
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "r"(m_addr + 8));
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(c2), "=r"(d) : "r"(m_addr + 16));
+    mw[0] = a; mw[1] = b; mw[2] = c2; mw[3] = d;
+  }
+}
+
 // Ragged rows: dS of this warp's 32 rows x 16 columns goes out through the
 // warp's transpose buffer, so each 2-byte store instruction writes 2 rows x 32
 // contiguous bytes instead of 32 scattered rows.
@@ -213,16 +309,68 @@ __device__ __forceinline__ void store_rag_dS_impl(const uint32_t (&o)[8], uint32
 #define store_rag_dS(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg) \
   store_rag_dS_impl<C::STG_PITCH>(o, stg, lane, prm, bhl, sq, skv, mb, q, c, cg)
 
-template <bool RAG, int MODE>
+// kRowsClass: a chunk goes out by TMA store (one 64 x 64 box per sub-class through the dS
+// class map) when every word of it belongs to the tile's rows: no padding rows, rows inside
+// the map, and the 64-column window inside the row.
+__device__ __forceinline__ bool cls_tma_store_ok(const ClsUnit& cu, int c, const Params& prm) {
+  const int col = c * BN - cu.s;
+  return !cu.pad && !cu.fallback && col >= 0 && col + BN <= prm.skv;
+}
+__device__ __forceinline__ void cls_tma_store(const CUtensorMap* tm, uint8_t* tile, const ClsUnit& cu, int c, int skv) {
+  const int col = c * BN - cu.s;
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    sm100::tma_store_2d(tm, tile + h * (BM * BN), (h ? cu.cls[1] : cu.cls[0]) * skv + col,
+                        int((cu.g0 + (h ? cu.rho[1] : cu.rho[0])) >> 4));
+}
+
+// kRowsClass: writes one finished 128 x 64 dS chunk from a 128B-swizzled staging tile.
+// Lane = (row lane/8 of 4, 16-byte word lane%8): 4 rows x 128 B per store instruction.
+// Every word is 16-byte aligned (the window starts at column -s); words that straddle a
+// row end (first chunk when s > 0, last chunk) go out element by element, and padding
+// rows (past the kv group) are skipped.
+__device__ __forceinline__ void cls_store_chunk(uint32_t tile, const ClsUnit& cu, int c, const Params& prm,
+                                                uint32_t lane) {
+  using namespace sm100;
+  const int rows = kGroups * prm.sq, skv = prm.skv;
+  const int j = int(lane & 7);
+  const int col = c * BN - cu.s + 8 * j;
+  if (col + 8 <= 0 || col >= skv) return;
+  const bool full = col >= 0 && col + 8 <= skv;
+#pragma unroll 4
+  for (int it = 0; it < BM / 4; ++it) {
+    const int i = 4 * it + int(lane >> 3);
+    const int rho = (i < 64 ? cu.rho[0] : cu.rho[1]) + 16 * (i & 63);
+    if (rho < rows) {
+      const uint4 v = lds128(tile + i * 128 + ((j ^ (i & 7)) << 4));
+      uint8_t* dst = prm.dS + 2 * ((unsigned long long)(cu.g0 + rho) * skv + col);
+      if (full) {
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else {
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (col + e >= 0 && col + e < skv)
+            reinterpret_cast<unsigned short*>(dst)[e] = (unsigned short)(wv[e >> 1] >> ((e & 1) * 16));
+      }
+    }
+  }
+}
+
+template <int RK, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64,1,128,1) SW128
           const __grid_constant__ CUtensorMap tm_V,    // (d, skv, b·8)  box (64,64,1)    SW128
-          const __grid_constant__ CUtensorMap tm_P,    // (skv, sq, bh)  box (64,128,1)   SW128 (aligned rows only)
-          const __grid_constant__ CUtensorMap tm_M,    // (skv, sq, bh)  box (64,128,1)   SW64 u8 (aligned only)
-          const __grid_constant__ CUtensorMap tm_dS,   // (skv, sq, bh)  box (64,128,1)   SW128 (aligned only)
+          const __grid_constant__ CUtensorMap tm_P,    // aligned: (skv, sq, bh) box (64,128,1) SW128;
+                                                       // class: (16·skv, rows/16) box (64,64) SW128
+          const __grid_constant__ CUtensorMap tm_M,    // aligned: (skv, sq, bh) box (64,128,1) SW64 u8;
+                                                       // class: u8 (16·skv, rows/16) box (80,64)
+          const __grid_constant__ CUtensorMap tm_dS,   // aligned: (skv, sq, bh) box (64,128,1) SW128;
+                                                       // class: as tm_P
           const Params prm) {
   using namespace sm100;
-  using C = Cfg<RAG, MODE>;
+  using C = Cfg<RK, MODE>;
+  constexpr bool RAG = C::RAG, CLS = C::CLS;
   constexpr int PST = C::PST, VST = C::VST, DOBUF = C::DOBUF;
   constexpr bool RES = C::RES, TP = C::TP, HOLD = C::HOLD, CP = C::CP;
   constexpr int NSLOT = C::NSLOT, SLOTC = C::SLOTC;
@@ -251,7 +399,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   const uint32_t lane = lane_id();
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < DOBUF; ++i) { mbar_init(&dO_full[i], 1); mbar_init(&dO_empty[i], 1); }
+    for (int i = 0; i < DOBUF; ++i) { mbar_init(&dO_full[i], CLS ? 32 : 1); mbar_init(&dO_empty[i], 1); }
     for (int i = 0; i < VST; ++i) { mbar_init(&V_full[i], 1); mbar_init(&V_empty[i], 1); }
     for (int i = 0; i < PST; ++i) {
       mbar_init(&PM_full[i], RAG ? 64 : 1);   // RAG: one cp.async completion arrive per producer lane (2 warps)
@@ -267,8 +415,10 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tm_dO); prefetch_tmap(&tm_V);
-    if (!RAG) { prefetch_tmap(&tm_P); prefetch_tmap(&tm_M); prefetch_tmap(&tm_dS); }
+    prefetch_tmap(&tm_V);
+    if (!CLS) prefetch_tmap(&tm_dO);
+    if (!RAG && !CLS) { prefetch_tmap(&tm_P); prefetch_tmap(&tm_M); prefetch_tmap(&tm_dS); }
+    if (CLS && prm.cls_Y > 0) { prefetch_tmap(&tm_P); prefetch_tmap(&tm_M); prefetch_tmap(&tm_dS); }
   }
   if (warp == 1) {
     tmem_alloc(tmem_base_slot, TSLOTS * BN);
@@ -297,16 +447,50 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     // ------------------------------------------------ dO / V producer (lane 0 issues)
     uint32_t vi = 0, di = 0;
     for (int u = cid; u < n_units; u += ncl) {
-      const int bhl = u / n_mb, mb = u - bhl * n_mb;
-      const int bh = prm.bh_base + bhl;
-      const int b = bh / kHeads, h = bh - b * kHeads;
-      const int zv = b * kKvHeads + h / kGroups;
+      int zv, vshift = 0;
       const int db = di % DOBUF;
       if (!warp_wait(&dO_empty[db], ((di / DOBUF) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
-        tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
-        tma_load_4d(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
+      if constexpr (CLS) {
+        // gather the tile's 128 dO rows (sub-class A rows 0..63, B rows 64..127) by 16-byte
+        // cp.async into the 128B-swizzled K-major layout a TMA box would produce
+        const ClsUnit cu = cls_unit(u, prm);
+        zv = cu.zv;
+        vshift = cu.s;
+        const int b = cu.ug / kKvHeads, kvh = cu.ug - b * kKvHeads;
+        const int rows = kGroups * sq;
+        // byte offsets of the 128 dO rows into a table (read back by this warp before each
+        // copy is issued, so the next unit may overwrite it)
+        unsigned long long* tab = reinterpret_cast<unsigned long long*>(smem + C::OFF_DOTAB);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int i = int(lane) + 32 * m;
+          int rho = (i < 64 ? cu.rho[0] : cu.rho[1]) + 16 * (i & 63);
+          if (rho >= rows) rho = cu.rho[0] < rows ? cu.rho[0] : 0;   // padding row: any valid row
+          const int hl = rho / sq, sqi = rho - hl * sq;
+          tab[i] = (((unsigned long long)b * sq + sqi) * kHeads + kvh * kGroups + hl) * (kHeadDim * 2);
+        }
+        __syncwarp();
+        const uint32_t base = smem_u32(smem + C::OFF_DO + db * DO_BYTES);
+        const int w = int(lane & 15), hf = w >> 3, j = w & 7;
+#pragma unroll 4
+        for (int it = 0; it < 64; ++it) {
+          const int i = 2 * it + int(lane >> 4);   // 16 lanes per row: 2 rows x 256 B per step
+          cp_async16(base + hf * (DO_BYTES / 2) + i * 128 + ((j ^ (i & 7)) << 4), prm.dO + tab[i] + w * 16);
+        }
+        // each lane's copies complete into dO_full (count 32); the MMA warp orders them
+        // before its tensor-core reads with a proxy fence
+        cp_async_arrive_noinc(&dO_full[db]);
+        __syncwarp();
+      } else {
+        const int bhl = u / n_mb, mb = u - bhl * n_mb;
+        const int bh = prm.bh_base + bhl;
+        const int b = bh / kHeads, h = bh - b * kHeads;
+        zv = b * kKvHeads + h / kGroups;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
+          tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
+          tma_load_4d(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
+        }
       }
       ++di;
       for (int pass = 0; pass < npass_mma; ++pass) {
@@ -317,14 +501,16 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           if (lane == 0) {
             mbar_arrive_expect_tx(&V_full[vs], V_BYTES);
             uint8_t* dst = smem + C::OFF_V + vs * V_BYTES;
-            tma_load_3d(dst, &tm_V, &V_full[vs], 0, c * BN, zv);
-            tma_load_3d(dst + V_BYTES / 2, &tm_V, &V_full[vs], 64, c * BN, zv);
+            // class rows: the window starts at column -s (V rows below 0 read as zeros)
+            tma_load_3d(dst, &tm_V, &V_full[vs], 0, c * BN - vshift, zv);
+            tma_load_3d(dst + V_BYTES / 2, &tm_V, &V_full[vs], 64, c * BN - vshift, zv);
           }
           ++vi;
         }
       }
     }
   producer_done:
+    if (CLS) cp_async_wait_all();
     // drain: the last issue of every stage must have landed before exit
     if (lane == 0) {
       for (uint32_t k = 0; k < uint32_t(DOBUF) && k < di; ++k) {
@@ -341,13 +527,56 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     // ------------------------------------------------ P / mask producer (RAG: warps 2 and 3)
     uint32_t pi = 0;
     for (int u = cid; u < n_units; u += ncl) {
-      const int bhl = u / n_mb, mb = u - bhl * n_mb;
+      const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
+      ClsUnit cu;
+      if constexpr (CLS) cu = cls_unit(u, prm);
       for (int pass = 0; pass < (TP ? 1 : 2); ++pass) {
         for (int cl = 0; cl < nloc; ++cl) {
           const int c = c0 + cl;
           const int ps = pi % PST;
           if (!warp_wait(&PM_empty[ps], ((pi / PST) & 1) ^ 1, abort_flag, err, 0x0103)) goto pm_done;
-          if constexpr (!RAG) {
+          if constexpr (CLS) {
+            uint8_t* pdst = smem + C::OFF_P + ps * C::P_BYTES;
+            uint8_t* mdst = smem + C::OFF_M + ps * C::M_BYTES;
+            const int col0 = c * BN - cu.s;   // window start column (a multiple of 8 elements from the row start's class offset)
+            if (!cu.fallback) {
+              // per sub-class: one P box (64 rows x 128 B, SW128) and one mask box (64 rows x 80 B)
+              if (lane == 0) mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
+              __syncwarp();
+              if (lane < 4) {
+                const int h = lane & 1;
+                const int y = int((cu.g0 + (h ? cu.rho[1] : cu.rho[0])) >> 4);
+                const int xe = (h ? cu.cls[1] : cu.cls[0]) * skv + col0;   // element offset inside the 16-row group
+                if (lane < 2)
+                  tma_load_2d(pdst + h * (C::P_BYTES / 2), &tm_P, &PM_full[ps], xe, y);
+                else
+                  tma_load_2d(mdst + h * (C::M_BYTES / 2), &tm_M, &PM_full[ps], xe - (h ? cu.mo[1] : cu.mo[0]), y);
+              }
+            } else {
+              // rows past the class maps' extent: 16-byte cp.async per row into the same layouts
+              // (P: 8 words, 128B swizzle; mask: 5 words at pitch 80), then complete at once
+              const uint32_t ps_u = smem_u32(pdst), ms_u = smem_u32(mdst);
+              const int w = int(lane & 15);
+              const int rows = kGroups * sq;
+              for (int it = 0; it < BM / 2; ++it) {
+                const int i = 2 * it + int(lane >> 4);
+                const int h = i >> 6;
+                const int rho = (h ? cu.rho[1] : cu.rho[0]) + 16 * (i & 63);
+                if (rho >= rows) continue;
+                const long long R = cu.g0 + rho;
+                if (w < 8) {
+                  const unsigned long long sp = (unsigned long long)(R * skv + col0) * 2 + 16ull * w;
+                  if (sp < prm.p_end16) cp_async16(ps_u + i * 128 + ((w ^ (i & 7)) << 4), prm.P + sp);
+                } else if (w < 13) {
+                  const unsigned long long sm_ = (unsigned long long)(R * skv + col0 - (h ? cu.mo[1] : cu.mo[0])) + 16ull * (w - 8);
+                  if (sm_ < prm.m_end16) cp_async16(ms_u + i * CLS_M_PITCH + (w - 8) * 16, prm.M + sm_);
+                }
+              }
+              cp_async_wait_all();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&PM_full[ps]);
+            }
+          } else if constexpr (!RAG) {
             if (lane == 0) {
               mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
               tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
@@ -396,6 +625,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     for (int u = cid; u < n_units; u += ncl) {
       const int db = di % DOBUF;
       if (!warp_wait(&dO_full[db], (di / DOBUF) & 1, abort_flag, err, 0x0201)) goto mma_done;
+      if (CLS) fence_proxy_async_smem();   // class rows: dO arrived by cp.async (generic proxy)
       const uint32_t a_base = smem_u32(smem + C::OFF_DO + db * DO_BYTES);
       for (int pass = 0; pass < npass_mma; ++pass) {
         for (int cl = 0; cl < nloc; ++cl) {
@@ -437,12 +667,38 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     if constexpr (!RAG && TP) {
       // kTmemP: dS of pass-2 chunk n is written into staging tile n % 2
       uint32_t n = 0;
+      bool tp_pend = false;   // class rows: a TMA store of the previous tile may be reading it
       for (int u = cid; u < n_units; u += ncl) {
-        const int bhl = u / n_mb, mb = u - bhl * n_mb;
+        const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
+        ClsUnit cu;
+        if constexpr (CLS) cu = cls_unit(u, prm);
         for (int cl = 0; cl < nloc; ++cl, ++n) {
           const int c = c0 + cl;
           const int b = n & 1;
           if (!warp_wait(&dS_ready[b], (n >> 1) & 1, abort_flag, err, 0x0306)) goto store_done_tp;
+          if constexpr (CLS) {
+            // plain stores here (kTmemP with class rows is only reached when forced); the
+            // previous tile's TMA store, if any, is waited for first
+            if (lane == 0 && n > 0) {
+              bulk_wait_read0();
+              if (tp_pend) mbar_arrive(&dS_free[b ^ 1]);
+            }
+            tp_pend = false;
+            __syncwarp();
+            if (!cls_tma_store_ok(cu, c, prm)) {
+              cls_store_chunk(smem_u32(smem + C::OFF_DST + b * (BM * BN * 2)), cu, c, prm, lane);
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&dS_free[b]);
+              continue;
+            }
+            if (lane == 0) {
+              cls_tma_store(&tm_dS, smem + C::OFF_DST + b * (BM * BN * 2), cu, c, skv);
+              bulk_commit();
+            }
+            tp_pend = true;
+            __syncwarp();
+            continue;
+          }
           if (lane == 0) {
             // one store may stay in flight while the epilogue fills the other staging tile
             tma_store_3d(&tm_dS, smem + C::OFF_DST + b * (BM * BN * 2), c * BN, mb * BM, bhl);
@@ -456,7 +712,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         }
       }
     store_done_tp:
-      if (lane == 0) {
+      if (lane == 0 && (!CLS || tp_pend)) {
         bulk_wait_read0();
         if (n > 0) mbar_arrive(&dS_free[(n - 1) & 1]);
         bulk_wait_all0();
@@ -466,16 +722,29 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       uint32_t pi = 0, dsr_par = 0;
       int npend = 0, pend0 = 0, pend1 = 0;   // stages whose store may still be reading (lane 0)
       for (int u = cid; u < n_units; u += ncl) {
-        const int bhl = u / n_mb, mb = u - bhl * n_mb;
+        const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
+        ClsUnit cu;
+        if constexpr (CLS) cu = cls_unit(u, prm);
         pi += nloc;  // pass-1 uses of the stages
         for (int cl = 0; cl < nloc; ++cl, ++pi) {
           const int c = c0 + cl;
           const int ps = pi % PST;
           if (!warp_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306)) goto store_done;
           dsr_par ^= 1u << ps;
+          if constexpr (CLS) {
+            if (!cls_tma_store_ok(cu, c, prm)) {
+              cls_store_chunk(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), cu, c, prm, lane);
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cnt(&PM_empty[ps], kEpiWarps);
+              continue;
+            }
+          }
           if (lane == 0) {
             // keep up to two stores in flight: a stage is freed once its store has read it
-            tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
+            if constexpr (CLS)
+              cls_tma_store(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, cu, c, skv);
+            else
+              tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
             bulk_commit();
             if (npend == 2) {
               bulk_wait_read<2>();
@@ -523,7 +792,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
 
     // Pass 1 of one chunk: row-sum contribution Σ m·dP~·P (the 1/(1-p) is applied once,
     // after the exchange).  kTmemP also parks the masked dP~ and P in TMEM for pass 2.
-    auto p1_chunk = [&](unsigned long long row_el, int cl, float& acc0, float& acc1) -> bool {
+    auto p1_chunk = [&](unsigned long long row_el, int cl, int cls_s, int mo, float& acc0, float& acc1) -> bool {
       const int c = c0 + cl;
       const int slot = job % NSLOT;
       if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0301)) return false;
@@ -541,21 +810,33 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) return false;
       const unsigned long long el = row_el + (unsigned long long)c * BN;
       uint32_t pw[8], mw[4], mx[4];
-      load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row,
-                    cg, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
+      if constexpr (CLS)
+        load_row_cls(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row,
+                     cg, mo, pw, mw);
+      else
+        load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row,
+                      cg, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
       expand_mask(mw, use_mask, mx);
-      const int nvalid = RAG ? min(max(skv - (c * BN + cg * CW), 0), CW) : CW;
-      if (RAG && nvalid < CW) {
-        // last, partial chunk only: columns >= seq_kv hold the next row's bytes
+      // valid columns e in [lo, hi) of this thread's 16: ragged rows end inside the last
+      // chunk; class windows also start s columns before the row in chunk 0
+      int lo = 0, hi = CW;
+      if constexpr (RAG) hi = min(max(skv - (c * BN + cg * CW), 0), CW);
+      if constexpr (CLS) {
+        const int cb = c * BN - cls_s + cg * CW;
+        lo = min(max(-cb, 0), CW);
+        hi = min(max(skv - cb, 0), CW);
+      }
+      if ((RAG || CLS) && (lo > 0 || hi < CW)) {
+        // columns outside the row hold other rows' bytes
 #pragma unroll
         for (int e = 0; e < 16; ++e)
-          if (e >= nvalid) mw[e >> 2] &= ~(0xFFu << ((e & 3) * 8));
+          if (e < lo || e >= hi) mw[e >> 2] &= ~(0xFFu << ((e & 3) * 8));
         if (!use_mask) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) mx[i] = 0;
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            if (e < nvalid) mx[e >> 2] |= 0xFFu << ((e & 3) * 8);
+            if (e >= lo && e < hi) mx[e >> 2] |= 0xFFu << ((e & 3) * 8);
         } else {
           expand_mask(mw, use_mask, mx);
         }
@@ -623,7 +904,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     };
 
     // Pass 2 of one chunk: dS = P · (m·dP~/(1-p) − r).
-    auto p2_chunk = [&](int bhl, int mb, unsigned long long row_el, int cl, uint32_t job0, float r) -> bool {
+    auto p2_chunk = [&](int bhl, int mb, unsigned long long row_el, int cl, int mo, uint32_t job0, float r) -> bool {
       const int c = c0 + cl;
       uint32_t o[8];
       if constexpr (TP) {
@@ -690,8 +971,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         const unsigned long long el = row_el + (unsigned long long)c * BN;
         const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
         uint32_t pw[8], mw[4], mx[4];
-        load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, uint32_t(el * 2) & 15u,
-                      uint32_t(el) & 15u, pw, mw);
+        if constexpr (CLS)
+          load_row_cls(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, mo, pw, mw);
+        else
+          load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, uint32_t(el * 2) & 15u,
+                        uint32_t(el) & 15u, pw, mw);
         expand_mask(mw, use_mask, mx);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -723,16 +1007,22 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     {
       uint32_t it = 0;
       for (int u = cid; u < n_units; u += ncl, ++it) {
-        const int bhl = u / n_mb, mb = u - bhl * n_mb;
-        const unsigned long long row_el = ((unsigned long long)bhl * sq + mb * BM + row) * skv;
+        const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
+        const unsigned long long row_el = CLS ? 0ull : ((unsigned long long)bhl * sq + mb * BM + row) * skv;
+        int cls_s = 0, mo = 0;
+        if constexpr (CLS) {
+          const ClsUnit cu = cls_unit(u, prm);
+          cls_s = cu.s;
+          mo = q >= 2 ? cu.mo[1] : cu.mo[0];   // TMEM lanes 0..63: sub-class A, 64..127: B
+        }
         const uint32_t job0 = job;
         float acc0 = 0.f, acc1 = 0.f, r;
         for (int cl = 0; cl < nloc; ++cl)
-          if (!p1_chunk(row_el, cl, acc0, acc1)) goto epi_done;
+          if (!p1_chunk(row_el, cl, cls_s, mo, acc0, acc1)) goto epi_done;
         if (TP || CP) tmem_wait_st();
         if (!exchange(acc0 + acc1, it, r)) goto epi_done;
         for (int cl = 0; cl < nloc; ++cl)
-          if (!p2_chunk(bhl, mb, row_el, cl, job0, r)) goto epi_done;
+          if (!p2_chunk(bhl, mb, row_el, cl, mo, job0, r)) goto epi_done;
       }
     }
   epi_done:

@@ -188,19 +188,23 @@ print("BAD" if bad else "OK", bad)
 """
 
 
+@pytest.mark.parametrize("rows", ["class", "ragged"])
 @pytest.mark.parametrize("mode", ["0", "1", "2", "3"])
-def test_every_ds_mode(mode, cuda):
+def test_every_ds_mode(mode, rows, cuda):
     """Each pass-2 mode of the dS kernel (recompute / resident / TMEM-held P / compact), forced
-    through ATTN_BWD_DS_MODE where the shape allows it, aligned and ragged rows, with and
-    without clusters, against the oracle (the variable is read once per process, hence
-    the subprocess)."""
+    through ATTN_BWD_DS_MODE where the shape allows it, aligned rows and both kernels for
+    rows that are not 16-byte multiples (class tiles / per-row re-aligning, forced through
+    ATTN_BWD_CLASS_ROWS / ATTN_BWD_RAGGED_ROWS), with and without clusters, against the
+    oracle (the variables are read once per process, hence the subprocess)."""
     import os
     import subprocess
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    shapes = [(1, 100, 192), (1, 70, 640), (1, 40, 1280), (1, 33, 467), (1, 21, 901), (1, 17, 3001)]
+    shapes = [(1, 100, 192), (1, 70, 640), (1, 40, 1280), (1, 33, 467), (1, 21, 901), (1, 17, 3001),
+              (2, 7, 29), (1, 205, 333)]
     code = _MODE_SCRIPT.format(root=root, pkg=os.path.join(root, "sol-1-advisor-token-fix_b200"), shapes=shapes)
     env = dict(os.environ, ATTN_BWD_DS_MODE=mode)
+    env["ATTN_BWD_CLASS_ROWS" if rows == "class" else "ATTN_BWD_RAGGED_ROWS"] = "1"
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip().startswith("OK"), r.stdout
@@ -257,3 +261,22 @@ def test_call_inside_caller_graph_capture(cuda):
     rS, rV = attn_bwd_reference(new)
     _close("dS", rS, dS)
     _close("dV", rV, dV)
+
+
+@pytest.mark.parametrize("shape", [(8, 128, 128), (4, 256, 256), (1, 512, 512), (2, 96, 467)])
+def test_repeated_calls_stress(shape, cuda):
+    """Hundreds of back-to-back full calls into NaN-filled outputs must all equal the first
+    result bit for bit (catches stage-reuse races that corrupt a few rows in rare calls)."""
+    bs, sq, skv = shape
+    data = _to(generate_input(bs, sq, skv, 70), cuda)
+    rS, rV = ab.custom_kernel(data)
+    out = (torch.empty_like(rS), torch.empty_like(rV))
+    bad = 0
+    for _ in range(400):
+        out[0].fill_(float("nan"))
+        out[1].fill_(float("nan"))
+        ab.attn_bwd(data, out=out)
+        bad += int(not (torch.equal(out[0], rS) and torch.equal(out[1], rV)))
+    torch.cuda.synchronize()
+    assert ab.poll_error() == 0
+    assert bad == 0, f"{bad} of 400 calls differed"
