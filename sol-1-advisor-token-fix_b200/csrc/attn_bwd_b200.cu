@@ -208,19 +208,21 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   const int nbh = s.n_units() * kGroups;
   if (nbh == 0 || s.sq == 0 || s.skv == 0) return ATTN_BWD_OK;
   // Rows whose length is not a multiple of 16 bytes: class tiles (16·64 rows per tile set)
-  // when they waste fewer row slots than 128-row blocks per head do, else the per-row
-  // re-aligning kernel.  Measured on B200 (dS us, class / per-row): c2 296 / 339,
-  // 32x691x773 2720 / 3730, 8x373x449 249 / 240, 4x211x293 88 / 62.
-  // ATTN_BWD_RAGGED_ROWS=1 / ATTN_BWD_CLASS_ROWS=1 force one of the two.
+  // unless they need over 10 % more row slots than 128-row blocks per head do, else the
+  // per-row re-aligning kernel.  Measured on B200 (dS us, class / per-row; slot ratio):
+  // c2 243 / 339 (0.80), 32x691x773 2264 / 3730 (0.93), 8x373x449 212 / 240 (1.07),
+  // 4x211x293 76 / 62 (1.20).
+  // ATTN_BWD_RAGGED_ROWS=1 / ATTN_BWD_CLASS_ROWS=1 force one of the two (the latter also
+  // for aligned rows, as a measurement of the class layout alone).
   static const bool force_ragged = std::getenv("ATTN_BWD_RAGGED_ROWS") != nullptr;
   static const bool force_class = std::getenv("ATTN_BWD_CLASS_ROWS") != nullptr;
   const bool rag = !tma_rows_ok(s.skv);
   int rk = ds::kRowsAligned;
-  if (rag) {
+  if (rag || force_class) {
     const long long per_class = (kGroups * (long long)s.sq + 15) / 16;
     const long long class_slots = (per_class + 63) / 64 * 64 * 16;
     const long long block_slots = (long long)kGroups * ((s.sq + ds::BM - 1) / ds::BM) * ds::BM;
-    rk = (force_class || (!force_ragged && class_slots < block_slots)) ? ds::kRowsClass : ds::kRowsRagged;
+    rk = (force_class || (!force_ragged && class_slots * 10 <= block_slots * 11)) ? ds::kRowsClass : ds::kRowsRagged;
   }
   const long long total_rows = (long long)nbh * s.sq;
   const long long cls_y = rk == ds::kRowsClass ? total_rows / 16 : 0;

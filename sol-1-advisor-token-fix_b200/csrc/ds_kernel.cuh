@@ -316,6 +316,10 @@ __device__ __forceinline__ bool cls_tma_store_ok(const ClsUnit& cu, int c, const
   const int col = c * BN - cu.s;
   return !cu.pad && !cu.fallback && col >= 0 && col + BN <= prm.skv;
 }
+__device__ __forceinline__ bool cls_tma_unit_ok(bool unit_ok, int c, int s, int skv) {
+  const int col = c * BN - s;
+  return unit_ok && col >= 0 && col + BN <= skv;
+}
 __device__ __forceinline__ void cls_tma_store(const CUtensorMap* tm, uint8_t* tile, const ClsUnit& cu, int c, int skv) {
   const int col = c * BN - cu.s;
 #pragma unroll
@@ -729,16 +733,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         for (int cl = 0; cl < nloc; ++cl, ++pi) {
           const int c = c0 + cl;
           const int ps = pi % PST;
+          // class rows: a row's first / last chunk is written by the epilogue threads
+          // themselves, which also free the stage
+          if (CLS && !cls_tma_store_ok(cu, c, prm)) continue;
           if (!warp_wait(&dS_ready[ps], (dsr_par >> ps) & 1u, abort_flag, err, 0x0306)) goto store_done;
           dsr_par ^= 1u << ps;
-          if constexpr (CLS) {
-            if (!cls_tma_store_ok(cu, c, prm)) {
-              cls_store_chunk(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), cu, c, prm, lane);
-              __syncwarp();
-              if (lane == 0) mbar_arrive_cnt(&PM_empty[ps], kEpiWarps);
-              continue;
-            }
-          }
           if (lane == 0) {
             // keep up to two stores in flight: a stage is freed once its store has read it
             if constexpr (CLS)
@@ -789,6 +788,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     const float scale = prm.scale;
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
     uint32_t job = 0, pi = 0, dsn = 0;
+    bool cls_tma_unit = false, cls_row_ok = false;   // class rows: per unit / per thread's row
+    int cls_s = 0;                                    // class rows: the unit's window shift
 
     // Pass 1 of one chunk: row-sum contribution Σ m·dP~·P (the 1/(1-p) is applied once,
     // after the exchange).  kTmemP also parks the masked dP~ and P in TMEM for pass 2.
@@ -984,7 +985,28 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
           o[k] = pack_bf16x2(p0 * fmaf(t0, scale, -r), p1 * fmaf(t1, scale, -r));
         }
-        if constexpr (!RAG) {
+        if (CLS && !cls_tma_unit_ok(cls_tma_unit, c, cls_s, skv)) {
+          // class rows, a row's first / last chunk: this thread's 16 values are two
+          // 16-byte aligned words of its row; words crossing the row end go element-wise
+          if (cls_row_ok) {
+            const int col0 = c * BN - cls_s + cg * CW;
+            uint8_t* dst = prm.dS + 2 * (row_el + col0);
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+              const int cw = col0 + 8 * w;
+              if (cw >= 0 && cw + 8 <= skv) {
+                *reinterpret_cast<uint4*>(dst + 16 * w) = make_uint4(o[4 * w], o[4 * w + 1], o[4 * w + 2], o[4 * w + 3]);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (cw + e >= 0 && cw + e < skv)
+                    reinterpret_cast<unsigned short*>(dst + 16 * w)[e] = (unsigned short)(o[4 * w + (e >> 1)] >> ((e & 1) * 16));
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&PM_empty[ps]);
+        } else if constexpr (!RAG) {
           // dS overwrites P in place (same swizzled positions); warp 3 stores the chunk
           const uint32_t p_row = p_stage + row * 128;
 #pragma unroll
@@ -1008,12 +1030,16 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       uint32_t it = 0;
       for (int u = cid; u < n_units; u += ncl, ++it) {
         const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
-        const unsigned long long row_el = CLS ? 0ull : ((unsigned long long)bhl * sq + mb * BM + row) * skv;
-        int cls_s = 0, mo = 0;
+        unsigned long long row_el = CLS ? 0ull : ((unsigned long long)bhl * sq + mb * BM + row) * skv;
+        int mo = 0;
         if constexpr (CLS) {
           const ClsUnit cu = cls_unit(u, prm);
           cls_s = cu.s;
           mo = q >= 2 ? cu.mo[1] : cu.mo[0];   // TMEM lanes 0..63: sub-class A, 64..127: B
+          cls_tma_unit = !cu.pad && !cu.fallback;
+          const int rho = (q >= 2 ? cu.rho[1] : cu.rho[0]) + 16 * (row & 63);
+          cls_row_ok = rho < kGroups * sq;
+          row_el = (unsigned long long)(cu.g0 + rho) * skv;   // flat element index of the row start
         }
         const uint32_t job0 = job;
         float acc0 = 0.f, acc1 = 0.f, r;
