@@ -13,7 +13,8 @@
 // overlaps the MMAs of the next.
 //
 // Roles: warp 0 producer, warp 1 MMA issuer + TMEM owner, warps 2..5 epilogue
-// (warp w drains TMEM lanes 32·(w%4)..).
+// (warp w drains TMEM lanes 32·(w%4)..); ragged rows add warps 6..13 (re-align) and
+// warp 14 (raw P_drop producer).
 //
 // Row formats (template flag RAG):
 //   RAG = false  seq_kv % 8 == 0: P_drop tiles are TMA tensor tiles (128B swizzle).
@@ -39,8 +40,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
 template <bool RAG>
 struct Cfg {
-  static constexpr int kThreads = RAG ? 448 : 192;    // RAG: + 8 re-align warps (6..13)
-  static constexpr int ST = RAG ? 4 : 6;               // operand stages
+  static constexpr int kThreads = RAG ? 480 : 192;    // RAG: + 8 re-align warps (6..13), raw producer (14)
+  static constexpr int ST = RAG ? 4 : 6;               // operand stages (RAG: 3 + 6 raw measured slower)
   static constexpr int RST = RAG ? 4 : 0;              // raw P_drop row stages
   static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack
   static constexpr int CLS_BYTES = 8 * RAW_PITCH;      // one class box: 8 rows (2176 B, 128-byte multiple)
@@ -144,7 +145,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
   int* err = prm.err;
 
   if (warp == 0) {
-    uint32_t si = 0, ri = 0;
+    uint32_t si = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int ul = u / n_jt, jt = u - ul * n_jt;
       const int ug = prm.unit_base + ul;
@@ -169,27 +170,6 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
             }
           }
           ++si;
-          if constexpr (RAG) {
-            const int rs = ri % RSTD;
-            if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1102)) goto prod_done;
-            uint8_t* rdst = smem + C::OFF_RAW + rs * C::RAW_BYTES;
-            const long long r0 = (long long)bhl * prm.sq + kc * BK;
-            if (r0 + min(BK, prm.sq - kc * BK) <= prm.tma_rows) {
-              if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], C::RAW_BYTES);
-              __syncwarp();
-              if (lane < 8) {
-                // class box `lane`: rows r0 + lane + 8i, i < 8 (row k of its 8-row group)
-                const long long rm = r0 + lane;
-                const unsigned long long off = ((unsigned long long)(rm & 7) * 2 * prm.skv + (unsigned long long)jt * 256) & ~15ull;
-                tma_load_2d(rdst + lane * C::CLS_BYTES, &tm_Pd, &raw_full[rs], int(off >> 2), int(rm >> 3));
-              }
-            } else {
-              raw_rows_sync(smem_u32(rdst), prm, bhl, kc, jt, lane);
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&raw_full[rs]);
-            }
-            ++ri;
-          }
         }
       }
     }
@@ -199,10 +179,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
         const uint32_t i = si - 1 - k;
         mbar_drain(&full[i % ST], (i / ST) & 1, err, 0x1111);
       }
-      for (uint32_t k = 0; RST > 0 && k < uint32_t(RSTD) && k < ri; ++k) {
-        const uint32_t i = ri - 1 - k;
-        mbar_drain(&raw_full[i % RSTD], (i / RSTD) & 1, err, 0x1112);
-      }
+
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -278,6 +255,46 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
     }
   }
 
+  else if (RAG && warp == 14) {
+    // raw P_drop producer: runs up to RST K chunks ahead of the re-align warps, independent
+    // of the operand ring (which waits for the MMA)
+    uint32_t ri = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int ul = u / n_jt, jt = u - ul * n_jt;
+      for (int g = 0; g < kGroups; ++g) {
+        const int bhl = ul * kGroups + g;
+        for (int kc = 0; kc < n_kc; ++kc, ++ri) {
+          const int rs = ri % RSTD;
+          if (!warp_wait(&raw_empty[rs], ((ri / RSTD) & 1) ^ 1, abort_flag, err, 0x1102)) goto raw_done;
+          uint8_t* rdst = smem + C::OFF_RAW + rs * C::RAW_BYTES;
+          const long long r0 = (long long)bhl * prm.sq + kc * BK;
+          if (r0 + min(BK, prm.sq - kc * BK) <= prm.tma_rows) {
+            if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], C::RAW_BYTES);
+            __syncwarp();
+            if (lane < 8) {
+              // class box `lane`: rows r0 + lane + 8i, i < 8 (row k of its 8-row group)
+              const long long rm = r0 + lane;
+              const unsigned long long off =
+                  ((unsigned long long)(rm & 7) * 2 * prm.skv + (unsigned long long)jt * 256) & ~15ull;
+              tma_load_2d(rdst + lane * C::CLS_BYTES, &tm_Pd, &raw_full[rs], int(off >> 2), int(rm >> 3));
+            }
+          } else {
+            raw_rows_sync(smem_u32(rdst), prm, bhl, kc, jt, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_full[rs]);
+          }
+        }
+      }
+    }
+  raw_done:
+    if (lane == 0) {
+      for (uint32_t k = 0; k < uint32_t(RSTD) && k < ri; ++k) {
+        const uint32_t i = ri - 1 - k;
+        mbar_drain(&raw_full[i % RSTD], (i / RSTD) & 1, err, 0x1112);
+      }
+    }
+    __syncwarp();
+  }
   else if (RAG) {
     // re-align warps 6..13: thread t handles one row r of the chunk and the 32-column
     // quarter qt = t / 64 (uniform per warp) of the 128-column tile.  Rows go diagonally
