@@ -131,8 +131,10 @@ def test_repeat_calls_deterministic(cuda):
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
 
 
-def test_shard_calls_match_full(cuda):
-    bs, sq, skv = 2, 96, 128
+@pytest.mark.parametrize("shape", [(2, 96, 128), (2, 96, 467), (3, 50, 333)])
+def test_shard_calls_match_full(shape, cuda):
+    """Sharded calls over (batch, kv-head) unit ranges reproduce the full call."""
+    bs, sq, skv = shape
     data = _to(generate_input(bs, sq, skv, 21), cuda)
     dS, dV = ab.custom_kernel(data)
     dO, P, Pd, V, M, p = data
@@ -140,7 +142,13 @@ def test_shard_calls_match_full(cuda):
         h0, h1 = u0 * 10, u1 * 10
         sl = lambda t: t.reshape(bs * 80, sq, skv)[h0:h1]
         sS, sV = ab.attn_bwd_shard((dO, sl(P), sl(Pd), V, sl(M), p), u0, u1)
-        assert torch.equal(sS, dS.reshape(bs * 80, sq, skv)[h0:h1])
+        if (h0 * sq * skv * 2) % 16 == 0:
+            # same row alignment as in the full call: same summation order, same bits
+            assert torch.equal(sS, dS.reshape(bs * 80, sq, skv)[h0:h1])
+        else:
+            # the shard is re-based by a copy; rows of seq_kv % 8 != 0 then shift their
+            # chunk windows differently (rounding-level differences only)
+            _close("shard dS", dS.reshape(bs * 80, sq, skv)[h0:h1].cpu(), sS)
         assert torch.equal(sV, dV.reshape(bs * 8, skv, 128)[u0:u1])
 
 
