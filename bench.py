@@ -291,6 +291,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-chunks", type=int, default=0, help="pipeline depth of the host-buffer call (0 = 16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--once", action="store_true",
                     help="one dS-kernel and one dV-kernel call on the config (for ncu), then exit")
@@ -365,20 +366,20 @@ def main():
     ds_gbs = mine["ds"] / t_ds / 1e9
     dv_gbs = mine["dv"] / t_dv / 1e9
 
-    # ---- end to end through the public API with host buffers (pinned), copies timed
+    # ---- end to end through the public API with host buffers (pinned), copies timed:
+    # attn_bwd_host pipelines chunks of units over H2D copies, kernels and D2H copies
     host = [t.cpu().pin_memory() for t in (dO, P, Pd, V, M)]
     h2d = sum(t.numel() * t.element_size() for t in host)
     dS_h = torch.empty((u1 - u0) * G, sq, skv, dtype=torch.bfloat16).pin_memory()
     dV_h = torch.empty(u1 - u0, skv, D, dtype=torch.bfloat16).pin_memory()
     d2h = dS_h.numel() * 2 + dV_h.numel() * 2
-    dev_in = [torch.empty_like(t, device=dev) for t in host]
+    work = tuple(torch.empty_like(t, device=dev) for t in host) + (
+        torch.empty_like(dS_h, device=dev), torch.empty_like(dV_h, device=dev))
+    host_data = tuple(host) + (p,)
 
     def e2e_step():
-        for d_, h_ in zip(dev_in, host):
-            d_.copy_(h_, non_blocking=True)
-        s_, v_ = ab.attn_bwd_shard(tuple(dev_in) + (p,), u0, u1)
-        dS_h.copy_(s_, non_blocking=True)
-        dV_h.copy_(v_, non_blocking=True)
+        ab.attn_bwd_host(host_data, u0, u1, work=work, out=(dS_h, dV_h), chunks=args.e2e_chunks,
+                         synchronize=False)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -387,6 +388,11 @@ def main():
     e2e_ms = timed_loop(e2e_step, args.e2e_steps, flush, stream)
     t_e2e = max_over_ranks(sum(e2e_ms) / 1e3, world)
     e2e_val = job["total"] * args.e2e_steps / t_e2e / 1e9
+    # the host-buffer results are the device call's (checked outside the timed region)
+    s_, v_ = step()
+    torch.cuda.synchronize()
+    assert torch.equal(dV_h, v_.cpu()) and torch.equal(dS_h[:2 * G], s_[:2 * G].cpu()), "host-buffer call mismatch"
+    del s_, v_
 
     # ---- gather of every rank's dS / dV shard to rank 0 (NCCL point-to-point), timed
     # separately: it is not part of the per-call kernel time the value reports

@@ -15,8 +15,8 @@
  *   grad_attn_scores      dS   [bs, 80, seq_q, seq_kv]   bf16 (output)
  *   grad_value_states     dV   [bs, 8, seq_kv, 128]      bf16 (output)
  *
- * All pointers are device pointers to contiguous tensors, 16-byte aligned.
- * Every call is asynchronous on `stream` and allocates nothing.  Returns 0 on
+ * All pointers are device pointers to contiguous tensors, 16-byte aligned (the host-buffer
+ * calls also take host pointers, named *_h).  Every call is asynchronous on `stream` and allocates nothing.  Returns 0 on
  * success or one of the ATTN_BWD_E* codes (nothing is launched on error).
  */
 #ifndef ATTN_BWD_B200_H
@@ -70,6 +70,40 @@ int attn_bwd_b200_ds_shard(const void* grad_attn_output, const void* attn_weight
 int attn_bwd_b200_dv_shard(const void* grad_attn_output, const void* attn_weights_dropped, int bs, int seq_q,
                            int seq_kv, int unit_begin, int unit_end, void* grad_value_states,
                            attn_bwd_stream_t stream);
+
+/* Host-buffer call: the same result as attn_bwd_b200_shard for inputs and outputs that live
+ * in HOST memory, for callers whose tensors are not yet on the GPU.  The reference's
+ * custom_kernel (starting_point.py:27-70) takes device tensors and has no such form; this
+ * is the end-to-end call of the multi-GPU split with the host<->device copies included.
+ *   *_h   host pointers with the shard layout of attn_bwd_b200_shard (dO_h and V_h whole,
+ *         P_h / Pd_h / M_h / dS_h from head 10*unit_begin, dV_h from slab unit_begin);
+ *         page-locked (cudaHostAlloc / pinned) memory lets the copies overlap; pageable
+ *         memory works but the copies then serialise with the host thread.
+ *   *_d   caller-allocated device buffers of the same sizes (16-byte aligned); the call
+ *         allocates nothing.  On return from the stream they hold the inputs and outputs.
+ *   chunks  pipeline depth: the unit range is cut into up to `chunks` pieces (0 = 16, at
+ *         most 64) on boundaries that keep every slice 16-byte aligned; chunk k's
+ *         host->device copies, kernels and device->host copies run on three streams, so the
+ *         two copy directions and the kernels overlap.
+ * Asynchronous on `stream`: all work starts after what is already queued there, and the
+ * stream waits for the last device->host copy.  Calls on one device are serialised on
+ * the host (the copy streams are per device). */
+int attn_bwd_b200_host_shard(const void* grad_attn_output_h, const void* attn_weights_h,
+                             const void* attn_weights_dropped_h, const void* value_states_h,
+                             const uint8_t* dropout_mask_h, float attention_dropout, int bs, int seq_q,
+                             int seq_kv, int unit_begin, int unit_end, void* grad_attn_scores_h,
+                             void* grad_value_states_h, void* grad_attn_output_d, void* attn_weights_d,
+                             void* attn_weights_dropped_d, void* value_states_d, uint8_t* dropout_mask_d,
+                             void* grad_attn_scores_d, void* grad_value_states_d, int chunks,
+                             attn_bwd_stream_t stream);
+/* Host-buffer call over all bs*8 units (unit_begin = 0, unit_end = bs*8). */
+int attn_bwd_b200_host(const void* grad_attn_output_h, const void* attn_weights_h,
+                       const void* attn_weights_dropped_h, const void* value_states_h,
+                       const uint8_t* dropout_mask_h, float attention_dropout, int bs, int seq_q, int seq_kv,
+                       void* grad_attn_scores_h, void* grad_value_states_h, void* grad_attn_output_d,
+                       void* attn_weights_d, void* attn_weights_dropped_d, void* value_states_d,
+                       uint8_t* dropout_mask_d, void* grad_attn_scores_d, void* grad_value_states_d, int chunks,
+                       attn_bwd_stream_t stream);
 
 /* Synchronises the current device, returns the code a kernel's bounded wait
  * recorded since the last poll (0 if none) and clears it.  The reference's

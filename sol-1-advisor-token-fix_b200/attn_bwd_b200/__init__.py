@@ -18,7 +18,7 @@ NUM_KEY_VALUE_HEADS = 8
 NUM_GROUPS = NUM_ATTENTION_HEADS // NUM_KEY_VALUE_HEADS
 HEAD_DIM = 128
 
-__all__ = ["custom_kernel", "attn_bwd", "attn_bwd_shard", "ds_shard", "dv_shard", "run",
+__all__ = ["custom_kernel", "attn_bwd", "attn_bwd_shard", "attn_bwd_host", "ds_shard", "dv_shard", "run",
            "AttnBwdError", "poll_error", "NUM_ATTENTION_HEADS", "NUM_KEY_VALUE_HEADS", "HEAD_DIM"]
 
 
@@ -111,6 +111,68 @@ def attn_bwd_shard(data, unit_begin, unit_end, out=None):
         _lib.call("attn_bwd_b200_shard", _ptr(dO), _ptr(P), _ptr(Pd), _ptr(V), _ptr(M), p,
                   bs, sq, skv, u0, u1, _ptr(dS), _ptr(dV), _stream())
     return dS, dV
+
+
+def attn_bwd_host(data, unit_begin=None, unit_end=None, device=None, work=None, out=None, chunks=0,
+                  synchronize=True):
+    """Attention backward for inputs and outputs in HOST memory, with the host<->device
+    copies pipelined against the kernels (C-ABI ``attn_bwd_b200_host_shard``).
+
+    ``data`` is the reference tuple of CPU tensors (contiguous, exact dtypes; pinned memory
+    lets the copies overlap).  With a unit range, attn_weights, attn_weights_dropped and
+    dropout_mask hold only the shard's heads, as in :func:`attn_bwd_shard`.  ``work`` is an
+    optional tuple of 7 device tensors (dO, P, P_drop, V, mask, dS, dV) of the same sizes,
+    reused across calls; otherwise they are allocated on ``device`` (default: current).
+    ``out`` optionally supplies the host (dS, dV) tensors.  Returns (dS, dV) on the host;
+    with ``synchronize=False`` they are valid only once the current stream has finished.
+    """
+    dO, P, Pd, V, M, p = data
+    for t, name in ((dO, "grad_attn_output"), (V, "value_states")):
+        if not isinstance(t, torch.Tensor) or t.device.type != "cpu":
+            raise TypeError(f"{name} must be a CPU tensor for attn_bwd_host")
+    bs, sq, skv = _shapes(dO, V)
+    u0 = 0 if unit_begin is None else unit_begin
+    u1 = bs * NUM_KEY_VALUE_HEADS if unit_end is None else unit_end
+    if not (0 <= u0 <= u1 <= bs * NUM_KEY_VALUE_HEADS):
+        raise ValueError(f"unit range [{u0},{u1}) outside [0,{bs * NUM_KEY_VALUE_HEADS}]")
+    nh = (u1 - u0) * NUM_GROUPS
+    full = unit_begin is None and unit_end is None
+    sshape = (bs, NUM_ATTENTION_HEADS, sq, skv) if full else (nh, sq, skv)
+    vshape = (bs, NUM_KEY_VALUE_HEADS, skv, HEAD_DIM) if full else (u1 - u0, skv, HEAD_DIM)
+    spec = [(dO, "grad_attn_output", torch.bfloat16, (bs, sq, NUM_ATTENTION_HEADS, HEAD_DIM)),
+            (P, "attn_weights", torch.bfloat16, sshape), (Pd, "attn_weights_dropped", torch.bfloat16, sshape),
+            (V, "value_states", torch.bfloat16, (bs, NUM_KEY_VALUE_HEADS, skv, HEAD_DIM)),
+            (M, "dropout_mask", torch.bool, sshape)]
+    for t, name, dt, shape in spec:
+        if not isinstance(t, torch.Tensor) or t.device.type != "cpu":
+            raise TypeError(f"{name} must be a CPU tensor for attn_bwd_host")
+        if t.dtype != dt or tuple(t.shape) != tuple(shape) or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous {dt} tensor of shape {tuple(shape)}, "
+                             f"got {t.dtype} {tuple(t.shape)}")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if work is None:
+        work = tuple(torch.empty(tuple(t.shape), dtype=t.dtype, device=dev) for t in (dO, P, Pd, V, M)) + (
+            torch.empty(sshape, dtype=torch.bfloat16, device=dev),
+            torch.empty(vshape, dtype=torch.bfloat16, device=dev))
+    if len(work) != 7:
+        raise ValueError("work must hold 7 device tensors (dO, P, P_drop, V, mask, dS, dV)")
+    sizes = [dO, P, Pd, V, M, P, None]
+    for w, ref in zip(work, sizes):
+        want = (ref.numel() * ref.element_size()) if ref is not None else (u1 - u0) * skv * HEAD_DIM * 2
+        if not w.is_cuda or not w.is_contiguous() or w.numel() * w.element_size() != want:
+            raise ValueError("work tensors must be contiguous CUDA tensors with the inputs' and outputs' sizes")
+    if out is None:
+        pin = torch.cuda.is_available()
+        dS_h = torch.empty(sshape, dtype=torch.bfloat16, pin_memory=pin)
+        dV_h = torch.empty(vshape, dtype=torch.bfloat16, pin_memory=pin)
+    else:
+        dS_h, dV_h = out
+    with torch.cuda.device(work[0].device):
+        _lib.call("attn_bwd_b200_host_shard", *(_ptr(t) for t in (dO, P, Pd, V, M)), float(p), bs, sq, skv, u0, u1,
+                  _ptr(dS_h), _ptr(dV_h), *(_ptr(w) for w in work), int(chunks), _stream())
+        if synchronize:
+            torch.cuda.current_stream().synchronize()
+    return dS_h, dV_h
 
 
 _BF16 = torch.bfloat16

@@ -44,6 +44,12 @@ struct DeviceState {
   GraphEntry graphs[16] = {};
   uint64_t graph_clock = 0;
   cudaStream_t cap = nullptr;   // private stream the captures run on
+  // Host-buffer calls (attn_bwd_b200_host_shard): copy-in and copy-out streams and the
+  // per-chunk events between the three stages (created on first use; never destroyed).
+  std::mutex host_mu;   // one host-buffer call at a time enqueues on these
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t h_fork = nullptr, h_join = nullptr;
+  cudaEvent_t in_done[64] = {}, comp_done[64] = {};
 };
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
@@ -600,6 +606,116 @@ int run_full(DeviceState* st, const Shape& s, const void* dO, const void* P, con
   return cudaGraphLaunch(exec, cs) == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 
+
+constexpr int kMaxHostChunks = 64;
+
+// Units per alignment step of a shard boundary: the smallest g in {1,2,4,8} for which an
+// offset of g units (10*g heads of sq*skv elements) is a multiple of 16 elements, so that
+// every per-chunk slice of P / P_drop / mask / dS starts 16-byte aligned and keeps the row
+// alignment classes of the whole call (the kernels then compute bit-identical rows).
+int unit_step(int sq, int skv) {
+  for (int g = 1; g < 8; g *= 2)
+    if (((long long)kGroups * g * sq * skv) % 16 == 0) return g;
+  return 8;
+}
+
+int make_host_resources(DeviceState* st) {
+  if (st->h2d) return ATTN_BWD_OK;
+  if (cudaStreamCreateWithFlags(&st->h2d, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&st->d2h, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&st->h_fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&st->h_join, cudaEventDisableTiming) != cudaSuccess)
+    return ATTN_BWD_ECUDA;
+  for (int k = 0; k < kMaxHostChunks; ++k)
+    if (cudaEventCreateWithFlags(&st->in_done[k], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&st->comp_done[k], cudaEventDisableTiming) != cudaSuccess)
+      return ATTN_BWD_ECUDA;
+  return ATTN_BWD_OK;
+}
+
+inline bool copy_async(void* dst, const void* src, size_t bytes, cudaMemcpyKind kind, cudaStream_t s) {
+  return bytes == 0 || cudaMemcpyAsync(dst, src, bytes, kind, s) == cudaSuccess;
+}
+
+// Host-buffer call as a three-stage pipeline over chunks of units:
+//   stream h2d:  copy chunk k's inputs host -> device (dO rows of the batches it first
+//                touches, its V slabs, its P / P_drop / mask heads), record in_done[k];
+//   stream cs:   wait in_done[k], run the dS + dV kernels on chunk k (dV on the side
+//                stream, joined back), record comp_done[k];
+//   stream d2h:  wait comp_done[k], copy chunk k's dS heads and dV slabs device -> host.
+// PCIe is full duplex and the copies of the two directions use separate copy engines, so
+// the call takes about max(H2D bytes, D2H bytes) / PCIe bandwidth plus one chunk of
+// latency, instead of the sum of both directions.  All three streams start after the work
+// already on cs (fork event) and cs waits for the last device -> host copy (join event).
+int run_host(DeviceState* st, const Shape& s, int chunks, const void* dO_h, const void* P_h, const void* Pd_h,
+             const void* V_h, const uint8_t* M_h, float p, void* dS_h, void* dV_h, void* dO_d, void* P_d,
+             void* Pd_d, void* V_d, uint8_t* M_d, void* dS_d, void* dV_d, cudaStream_t cs) {
+  const int n_units = s.n_units();
+  if (n_units == 0) return ATTN_BWD_OK;
+  std::lock_guard<std::mutex> lk(st->host_mu);
+  int rc = make_host_resources(st);
+  if (rc) return rc;
+  const int g = unit_step(s.sq, s.skv);
+  // chunk boundaries are multiples of g units from unit_begin (which the caller's own
+  // shard layout already aligns); a chunk never holds fewer than g units
+  const int steps = (n_units + g - 1) / g;
+  if (chunks <= 0) chunks = 16;
+  if (chunks > kMaxHostChunks) chunks = kMaxHostChunks;
+  if (chunks > steps) chunks = steps;
+  const size_t head_elems = (size_t)s.sq * s.skv;                       // one head of P / mask / dS
+  const size_t slab_elems = (size_t)s.skv * kHeadDim;                   // one unit of V / dV
+  const size_t row_elems = (size_t)s.sq * kHeads * kHeadDim;            // one batch row of dO
+  if (cudaEventRecord(st->h_fork, cs) != cudaSuccess || cudaStreamWaitEvent(st->h2d, st->h_fork, 0) != cudaSuccess ||
+      cudaStreamWaitEvent(st->d2h, st->h_fork, 0) != cudaSuccess)
+    return ATTN_BWD_ECUDA;
+  int next_batch = 0;   // dO batch rows [0, next_batch) of the touched range are copied
+  bool dO_any = false;
+  for (int k = 0; k < chunks && rc == ATTN_BWD_OK; ++k) {
+    // chunk k: units [a, b) relative to unit_begin, split as evenly as the step allows
+    const int a = (int)((long long)steps * k / chunks) * g;
+    int b = (int)((long long)steps * (k + 1) / chunks) * g;
+    if (b > n_units) b = n_units;
+    const int ua = s.u0 + a, ub = s.u0 + b;
+    // ---- inputs
+    const int b_lo = ua / kKvHeads, b_hi = (ub - 1) / kKvHeads + 1;   // batch rows this chunk reads
+    int c_lo = dO_any && b_lo < next_batch ? next_batch : b_lo;
+    bool ok = true;
+    if (b_hi > c_lo) {
+      const size_t off = (size_t)c_lo * row_elems * 2, bytes = (size_t)(b_hi - c_lo) * row_elems * 2;
+      ok = copy_async((char*)dO_d + off, (const char*)dO_h + off, bytes, cudaMemcpyHostToDevice, st->h2d);
+      next_batch = b_hi;
+      dO_any = true;
+    }
+    const size_t h_off = (size_t)a * kGroups * head_elems, h_n = (size_t)(b - a) * kGroups * head_elems;
+    const size_t v_off = (size_t)ua * slab_elems, v_n = (size_t)(b - a) * slab_elems;
+    ok = ok && copy_async((char*)V_d + v_off * 2, (const char*)V_h + v_off * 2, v_n * 2, cudaMemcpyHostToDevice, st->h2d);
+    ok = ok && copy_async((char*)P_d + h_off * 2, (const char*)P_h + h_off * 2, h_n * 2, cudaMemcpyHostToDevice, st->h2d);
+    ok = ok && copy_async((char*)Pd_d + h_off * 2, (const char*)Pd_h + h_off * 2, h_n * 2, cudaMemcpyHostToDevice,
+                          st->h2d);
+    ok = ok && copy_async(M_d + h_off, M_h + h_off, h_n, cudaMemcpyHostToDevice, st->h2d);
+    ok = ok && cudaEventRecord(st->in_done[k], st->h2d) == cudaSuccess;
+    // ---- kernels
+    ok = ok && cudaStreamWaitEvent(cs, st->in_done[k], 0) == cudaSuccess;
+    if (!ok) { rc = ATTN_BWD_ECUDA; break; }
+    const Shape cs_shape{s.bs, s.sq, s.skv, ua, ub};
+    rc = enqueue_full(st, cs_shape, dO_d, (const char*)P_d + h_off * 2, (const char*)Pd_d + h_off * 2, V_d,
+                      M_d + h_off, p, (char*)dS_d + h_off * 2, (char*)dV_d + (size_t)a * slab_elems * 2, cs);
+    if (rc) break;
+    // ---- outputs
+    ok = cudaEventRecord(st->comp_done[k], cs) == cudaSuccess &&
+         cudaStreamWaitEvent(st->d2h, st->comp_done[k], 0) == cudaSuccess &&
+         copy_async((char*)dS_h + h_off * 2, (const char*)dS_d + h_off * 2, h_n * 2, cudaMemcpyDeviceToHost, st->d2h) &&
+         copy_async((char*)dV_h + (size_t)a * slab_elems * 2, (const char*)dV_d + (size_t)a * slab_elems * 2,
+                    v_n * 2, cudaMemcpyDeviceToHost, st->d2h);
+    if (!ok) rc = ATTN_BWD_ECUDA;
+  }
+  // join even after an error, so cs never runs ahead of issued copies
+  if (cudaEventRecord(st->h_join, st->h2d) != cudaSuccess || cudaStreamWaitEvent(cs, st->h_join, 0) != cudaSuccess ||
+      cudaEventRecord(st->h_join, st->d2h) != cudaSuccess || cudaStreamWaitEvent(cs, st->h_join, 0) != cudaSuccess)
+    return rc ? rc : ATTN_BWD_ECUDA;
+  return rc;
+}
+
 }  // namespace
 
 extern "C" {
@@ -649,6 +765,33 @@ int attn_bwd_b200(const void* dO, const void* P, const void* Pd, const void* V, 
   return attn_bwd_b200_shard(dO, P, Pd, V, M, p, bs, sq, skv, 0, bs * kKvHeads, dS, dV, stream);
 }
 
+int attn_bwd_b200_host_shard(const void* dO_h, const void* P_h, const void* Pd_h, const void* V_h, const uint8_t* M_h,
+                             float p, int bs, int sq, int skv, int u0, int u1, void* dS_h, void* dV_h, void* dO_d,
+                             void* P_d, void* Pd_d, void* V_d, uint8_t* M_d, void* dS_d, void* dV_d, int chunks,
+                             attn_bwd_stream_t stream) {
+  Shape s{bs, sq, skv, u0, u1};
+  DeviceState* st = nullptr;
+  int rc = prologue(&st, s);
+  if (rc) return rc;
+  if (chunks < 0) return ATTN_BWD_EINVAL;
+  const void* all[] = {dO_h, P_h, Pd_h, V_h, M_h, dS_h, dV_h, dO_d, P_d, Pd_d, V_d, M_d, dS_d, dV_d};
+  const long long n[] = {s.n_dO(), s.n_scores(), s.n_scores(), s.n_V(), s.n_scores(), s.n_scores(), s.n_dV(),
+                         s.n_dO(), s.n_scores(), s.n_scores(), s.n_V(), s.n_scores(), s.n_scores(), s.n_dV()};
+  for (int i = 0; i < 14; ++i)
+    if (!ptr_ok(all[i], n[i])) return ATTN_BWD_EINVAL;
+  for (int i = 7; i < 14; ++i)
+    if (!aligned16(all[i])) return ATTN_BWD_EALIGN;
+  return run_host(st, s, chunks, dO_h, P_h, Pd_h, V_h, M_h, p, dS_h, dV_h, dO_d, P_d, Pd_d, V_d, M_d, dS_d, dV_d,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+int attn_bwd_b200_host(const void* dO_h, const void* P_h, const void* Pd_h, const void* V_h, const uint8_t* M_h,
+                       float p, int bs, int sq, int skv, void* dS_h, void* dV_h, void* dO_d, void* P_d, void* Pd_d,
+                       void* V_d, uint8_t* M_d, void* dS_d, void* dV_d, int chunks, attn_bwd_stream_t stream) {
+  return attn_bwd_b200_host_shard(dO_h, P_h, Pd_h, V_h, M_h, p, bs, sq, skv, 0, bs * kKvHeads, dS_h, dV_h, dO_d, P_d,
+                                  Pd_d, V_d, M_d, dS_d, dV_d, chunks, stream);
+}
+
 int attn_bwd_b200_selftest_wait_timeout(int limit_us, attn_bwd_stream_t stream) {
   DeviceState* st = nullptr;
   int rc = device_state(&st);
@@ -684,7 +827,7 @@ const char* attn_bwd_b200_strerror(int code) {
   }
 }
 
-int attn_bwd_b200_version(void) { return 100; }
+int attn_bwd_b200_version(void) { return 101; }
 
 #ifdef ATTN_BWD_WAIT_STATS
 // Diagnostics builds only (not part of the ABI): copies and clears the per-site wait cycles.

@@ -71,3 +71,17 @@ def test_torch_binding_loads_and_declines_cpu_tensors():
     V = torch.zeros(1, 8, 8, 128, dtype=torch.bfloat16)
     M = torch.zeros(1, 80, 4, 8, dtype=torch.bool)
     assert ab._torch_fast_fn(dO, P, P, V, M, 0.1) is None
+
+
+def test_host_call_argument_errors_without_gpu():
+    import torch
+    import attn_bwd_b200 as ab
+    from attn_bwd_b200.generate import generate_input
+    data = generate_input(1, 4, 16, seed=1, device="cpu")
+    bad = (data[0].float(),) + tuple(data[1:])
+    with pytest.raises(ValueError):
+        ab.attn_bwd_host(bad)
+    with pytest.raises(ValueError):
+        ab.attn_bwd_host(data, 0, 9)
+    with pytest.raises(TypeError):
+        ab.attn_bwd_host((None,) + tuple(data[1:]))
