@@ -332,6 +332,13 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.resident = mode != ds::kRecompute;
   prm.bh_base = s.u0 * kGroups;
   prm.use_mask = p > 0.f ? 1 : 0;
+  // L2 prefetch of a CTA's next unit during pass 2 (aligned rows only): measured on B200
+  // over the SOL-ExecBench shapes and c1-c4, it helps rows of up to 6 chunks held by one
+  // CTA (c1 dS 97 -> 91 us, 64x128x128 161 -> 155 us) and hurts longer rows (c4 dS
+  // 2010 -> 2096 us, 1x4096x4096 +5 %), where the extra L2 footprint evicts pass-2 data.
+  // ATTN_BWD_L2PF=0/1 forces it off / on (measurements).
+  static const int l2pf_env = std::getenv("ATTN_BWD_L2PF") ? std::atoi(std::getenv("ATTN_BWD_L2PF")) : -1;
+  prm.l2pf = l2pf_env >= 0 ? l2pf_env : (prm.cs == 1 && prm.nchunks <= 6 ? 1 : 0);
   prm.scale = p > 0.f ? 1.0f / (1.0f - p) : 1.0f;
   prm.err = st.err;
   prm.P = static_cast<const uint8_t*>(P);

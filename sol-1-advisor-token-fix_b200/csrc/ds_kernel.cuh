@@ -136,6 +136,7 @@ struct Params {
   int resident;     // 1: pass 2 re-reads pass-1 TMEM columns
   int bh_base;      // global (batch·head) index of local head 0
   int use_mask;     // p > 0
+  int l2pf;         // aligned rows, two passes: L2 prefetch of the next unit during pass 2
   float scale;      // 1/(1-p) when use_mask, else 1
   int* err;
   // raw pointers for the RAG path (local shard bases, 16-byte aligned)
@@ -585,6 +586,14 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
               mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
               tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
               tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
+              // pass 2 re-reads this unit from L2, which leaves HBM idle for this CTA: pull
+              // the same chunk of the CTA's next unit into L2 meanwhile, so that unit's
+              // pass 1 finds it there
+              if (pass == 1 && prm.l2pf && u + ncl < n_units) {
+                const int un = u + ncl, bn_ = un / n_mb, mbn = un - bn_ * n_mb;
+                tma_prefetch_l2_3d(&tm_P, c * BN, mbn * BM, bn_);
+                tma_prefetch_l2_3d(&tm_M, c * BN, mbn * BM, bn_);
+              }
             }
           } else {
             // 16-byte cp.async of the aligned words covering each row segment: 9 for P,
