@@ -137,6 +137,7 @@ struct Params {
   int bh_base;      // global (batch·head) index of local head 0
   int use_mask;     // p > 0
   int l2pf;         // aligned rows, two passes: L2 prefetch of the next unit during pass 2
+  int l2hint;       // aligned rows: L2 eviction hints (pass-1 tiles kept, pass-2 tiles and dS evicted first)
   float scale;      // 1/(1-p) when use_mask, else 1
   int* err;
   // raw pointers for the RAG path (local shard bases, 16-byte aligned)
@@ -584,8 +585,15 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           } else if constexpr (!RAG) {
             if (lane == 0) {
               mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
-              tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
-              tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
+              if (prm.l2hint) {
+                // pass 1's tiles are read again by pass 2 (keep them); pass 2 is their last use
+                const uint64_t pol = (pass == 0 && !TP) ? policy_evict_last() : policy_evict_first();
+                tma_load_3d_hint(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl, pol);
+                tma_load_3d_hint(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl, pol);
+              } else {
+                tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
+                tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
+              }
               // pass 2 re-reads this unit from L2, which leaves HBM idle for this CTA: pull
               // the same chunk of the CTA's next unit into L2 meanwhile, so that unit's
               // pass 1 finds it there
@@ -752,7 +760,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
             if constexpr (CLS)
               cls_tma_store(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, cu, c, skv);
             else
-              tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
+              if (prm.l2hint)   // dS is not read again: do not let it push P / mask out of L2
+                tma_store_3d_hint(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl,
+                                  policy_evict_first());
+              else
+                tma_store_3d(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl);
             bulk_commit();
             if (npend == 2) {
               bulk_wait_read<2>();
