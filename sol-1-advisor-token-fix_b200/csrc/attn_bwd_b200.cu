@@ -343,7 +343,8 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   // and dS stores evicted first): measured on B200, c3 dS 1279 -> 1245 us, c1 96 -> 91 us,
   // c4 unchanged.  ATTN_BWD_L2HINT=0 turns them off (measurements).
   static const int l2hint_env = std::getenv("ATTN_BWD_L2HINT") ? std::atoi(std::getenv("ATTN_BWD_L2HINT")) : 1;
-  prm.l2hint = l2hint_env;
+  // class rows: ATTN_BWD_L2HINT=2 (measurement) also applies them there
+  prm.l2hint = rk == ds::kRowsClass ? (l2hint_env == 2 ? 1 : 0) : (l2hint_env != 0 ? 1 : 0);
   prm.scale = p > 0.f ? 1.0f / (1.0f - p) : 1.0f;
   prm.err = st.err;
   prm.P = static_cast<const uint8_t*>(P);

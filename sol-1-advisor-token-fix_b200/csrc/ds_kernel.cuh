@@ -322,12 +322,18 @@ __device__ __forceinline__ bool cls_tma_unit_ok(bool unit_ok, int c, int s, int 
   const int col = c * BN - s;
   return unit_ok && col >= 0 && col + BN <= skv;
 }
-__device__ __forceinline__ void cls_tma_store(const CUtensorMap* tm, uint8_t* tile, const ClsUnit& cu, int c, int skv) {
+__device__ __forceinline__ void cls_tma_store(const CUtensorMap* tm, uint8_t* tile, const ClsUnit& cu, int c, int skv,
+                                              bool hint = false) {
   const int col = c * BN - cu.s;
+  const uint64_t pol = hint ? sm100::policy_evict_first() : 0;
 #pragma unroll
-  for (int h = 0; h < 2; ++h)
-    sm100::tma_store_2d(tm, tile + h * (BM * BN), (h ? cu.cls[1] : cu.cls[0]) * skv + col,
-                        int((cu.g0 + (h ? cu.rho[1] : cu.rho[0])) >> 4));
+  for (int h = 0; h < 2; ++h) {
+    const int x = (h ? cu.cls[1] : cu.cls[0]) * skv + col, y = int((cu.g0 + (h ? cu.rho[1] : cu.rho[0])) >> 4);
+    if (hint)
+      sm100::tma_store_2d_hint(tm, tile + h * (BM * BN), x, y, pol);
+    else
+      sm100::tma_store_2d(tm, tile + h * (BM * BN), x, y);
+  }
 }
 
 // kRowsClass: writes one finished 128 x 64 dS chunk from a 128B-swizzled staging tile.
@@ -553,10 +559,19 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
                 const int h = lane & 1;
                 const int y = int((cu.g0 + (h ? cu.rho[1] : cu.rho[0])) >> 4);
                 const int xe = (h ? cu.cls[1] : cu.cls[0]) * skv + col0;   // element offset inside the 16-row group
-                if (lane < 2)
+                if (prm.l2hint) {
+                  // as on the aligned path: pass-1 tiles kept for pass 2, pass-2 reloads evicted first
+                  const uint64_t pol = (pass == 0 && !TP) ? policy_evict_last() : policy_evict_first();
+                  if (lane < 2)
+                    tma_load_2d_hint(pdst + h * (C::P_BYTES / 2), &tm_P, &PM_full[ps], xe, y, pol);
+                  else
+                    tma_load_2d_hint(mdst + h * (C::M_BYTES / 2), &tm_M, &PM_full[ps], xe - (h ? cu.mo[1] : cu.mo[0]),
+                                     y, pol);
+                } else if (lane < 2) {
                   tma_load_2d(pdst + h * (C::P_BYTES / 2), &tm_P, &PM_full[ps], xe, y);
-                else
+                } else {
                   tma_load_2d(mdst + h * (C::M_BYTES / 2), &tm_M, &PM_full[ps], xe - (h ? cu.mo[1] : cu.mo[0]), y);
+                }
               }
             } else {
               // rows past the class maps' extent: 16-byte cp.async per row into the same layouts
@@ -758,7 +773,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           if (lane == 0) {
             // keep up to two stores in flight: a stage is freed once its store has read it
             if constexpr (CLS)
-              cls_tma_store(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, cu, c, skv);
+              cls_tma_store(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, cu, c, skv, prm.l2hint != 0);
             else
               if (prm.l2hint)   // dS is not read again: do not let it push P / mask out of L2
                 tma_store_3d_hint(&tm_dS, smem + C::OFF_P + ps * C::P_BYTES, c * BN, mb * BM, bhl,
