@@ -64,13 +64,26 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def shard_range(n_units, rank, world):
-    return n_units * rank // world, n_units * (rank + 1) // world
+def shard_range(n_units, rank, world, sq, skv):
+    from attn_bwd_b200.shard import unit_range
+    return unit_range(n_units, rank, world, sq, skv)
+
+
+def _generate_module():
+    """attn_bwd_b200/generate.py loaded by file path: the input generator without the
+    package (whose import maps the CUDA library), for the CPU-only reference arm."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "_attn_bwd_generate", os.path.join(PKG_DIR, "attn_bwd_b200", "generate.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def make_shard_inputs(bs, sq, skv, u0, u1, seed, device):
-    """Full dO and V, and P / P_drop / mask for heads of units [u0, u1) only."""
-    from attn_bwd_b200.generate import generate_input
+    """Full dO and V, and P / P_drop / mask for heads of units [u0, u1) only.  Batch row b
+    is drawn on `device` with seed seed*1000 + b."""
+    generate_input = _generate_module().generate_input
     nh = (u1 - u0) * G
     dO = torch.empty(bs, sq, H, D, dtype=torch.bfloat16, device=device)
     V = torch.empty(bs, KVH, skv, D, dtype=torch.bfloat16, device=device)
@@ -162,21 +175,37 @@ def max_over_ranks(x, world):
     return t.item()
 
 
+def unit_inputs(cfg, n_units_max=8):
+    """CPU copies of the bench workload's own first (batch, kv-head) units: batch row 0 of
+    the config drawn exactly as the GPU arm draws it (make_shard_inputs: seed
+    (1000 + config index) * 1000, on the GPU when there is one), cut into per-unit tuples
+    of the reference layout (10 heads each)."""
+    gen = _generate_module()
+    bs, sq, skv = CONFIGS[cfg]
+    seed = (1000 + int(cfg[1])) * 1000
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    d = gen.generate_input(1, sq, skv, seed, device=dev)
+    d = tuple(t.cpu() if isinstance(t, torch.Tensor) else t for t in d)
+    units = []
+    for kvh in range(min(KVH, n_units_max)):
+        hs = slice(kvh * G, kvh * G + G)
+        units.append((d[0][:, :, hs].contiguous(), d[1][:, hs].contiguous(), d[2][:, hs].contiguous(),
+                      d[3][:, kvh:kvh + 1].contiguous(), d[4][:, hs].contiguous(), d[5]))
+    return units, dev
+
+
 def cpu_sample(cfg, units_target_s=12.0, max_units=100000):
-    """Times the CPU oracle on whole (batch, kv-head) units of the config until
+    """Times the CPU oracle on whole (batch, kv-head) units of the config's own inputs until
     about `units_target_s` seconds have passed.  Returns (GB/s, units, seconds)."""
-    from attn_bwd_b200.generate import generate_input
     from oracle.attn_bwd_oracle import _attn_bwd_group
     bs, sq, skv = CONFIGS[cfg]
     torch.set_num_threads(os.cpu_count() or 1)
-    d = generate_input(1, sq, skv, 4242)
-    sub = (d[0][:, :, :G].contiguous(), d[1][:, :G].contiguous(), d[2][:, :G].contiguous(),
-           d[3][:, :1].contiguous(), d[4][:, :G].contiguous(), d[5])
-    _attn_bwd_group(sub)  # warm-up
+    units, _ = unit_inputs(cfg)
+    _attn_bwd_group(units[0])  # warm-up
     n, t_total = 0, 0.0
     while t_total < units_target_s and n < max_units:
         t0 = time.perf_counter()
-        _attn_bwd_group(sub)
+        _attn_bwd_group(units[n % len(units)])
         t_total += time.perf_counter() - t0
         n += 1
     gbs = alg_bytes(n, sq, skv)["total"] / t_total / 1e9
@@ -184,38 +213,42 @@ def cpu_sample(cfg, units_target_s=12.0, max_units=100000):
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the path (the oracle restatement of
+    starting_point.py:27-70; PyTorch fp32 on all host threads) on whole (batch, kv-head)
+    units of the config's own inputs.  Loads neither the package nor its CUDA library."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     bs, sq, skv = CONFIGS[args.config]
-    from attn_bwd_b200.generate import generate_input
     from oracle.attn_bwd_oracle import _attn_bwd_group
     torch.set_num_threads(os.cpu_count() or 1)
-    d = generate_input(1, sq, skv, 4242)
-    sub = (d[0][:, :, :G].contiguous(), d[1][:, :G].contiguous(), d[2][:, :G].contiguous(),
-           d[3][:, :1].contiguous(), d[4][:, :G].contiguous(), d[5])
+    units, gen_dev = unit_inputs(args.config)
     units_per_step = 2
+    k = 0
     for _ in range(args.warmup):
         for _u in range(units_per_step):
-            _attn_bwd_group(sub)
+            _attn_bwd_group(units[k % len(units)])
+            k += 1
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
         for _u in range(units_per_step):
-            _attn_bwd_group(sub)
+            _attn_bwd_group(units[k % len(units)])
+            k += 1
         times.append(time.perf_counter() - t0)
     t = sum(times)
     gbs = alg_bytes(units_per_step * args.steps, sq, skv)["total"] / t / 1e9
     n_units = bs * KVH
     us_call = (t / (units_per_step * args.steps)) * n_units * 1e6
     cores = torch.get_num_threads()
-    sample = f"{units_per_step} of {n_units} (batch, kv-head) units of {args.config} per step"
+    sample = (f"{units_per_step} of {n_units} (batch, kv-head) units of {args.config} per step, cycling over "
+              f"units 0-{len(units) - 1} of the bench's own seeded inputs (batch row 0, drawn on {gen_dev})")
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 3), "us_per_call": round(us_call, 1),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, eval_modal_attn_bwd.py:139-169 distribution)",
-            "config": {"workload": f"{args.config} bs={bs} seq_q={sq} seq_kv={skv} heads=80/8 d=128 p=0.1",
+            "config": {"workload": f"{args.config}: bs={bs} seq_q={sq} seq_kv={skv} heads=80/8 d=128 p=0.1",
                        "sample": sample},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                              "sample": sample},
@@ -229,44 +262,80 @@ SOL_SHAPES = [(4, 256, 256), (8, 373, 449), (4, 1024, 2048), (64, 128, 128), (2,
               (1, 4096, 4096)]
 
 
+def _time_like_evaluator(fn, data, flush, reps, warmup):
+    """eval_modal_attn_bwd.py:365-401: warm-up calls, then per rep an L2 flush, a
+    synchronize and CUDA events around the call (host time of the call counts)."""
+    for _ in range(max(warmup, 3)):
+        fn(data)
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(reps):
+        flush.fill_(42)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn(data)
+        e1.record()
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    return sum(ms) / len(ms) * 1e3
+
+
+def _load_snapshot(path):
+    """A reference submission file loaded the way the evaluator loads one
+    (eval_modal_attn_bwd.py:238-247): importlib from its path, module name "submission"."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("submission", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.custom_kernel
+
+
 def run_sol_sweep(args):
     """The 16 SOL-ExecBench shapes (eval_modal_attn_bwd.py:18-35, sizes only), each timed
-    the way the reference evaluator does (eval_modal_attn_bwd.py:365-401): warm-up calls,
-    then per rep an L2 flush (256 MiB fill), a synchronize, and CUDA events around
-    custom_kernel (so host-side time of the call counts, as it does there).  Prints one
-    JSON line with per-shape µs, the geomean and the reference's score 756/geomean."""
+    the way the reference evaluator does (eval_modal_attn_bwd.py:365-401).  With
+    --snapshot PATH the reference submission at PATH (unmodified) is timed the same way on
+    the same GPU and inputs, alternating with this library shape by shape, and its outputs
+    are compared with ours (allclose at the evaluator's 1e-2).  Prints one JSON line with
+    per-shape us, both geomeans, the per-shape ratio and the reference's score
+    756/geomean (eval_modal_attn_bwd.py:417-420)."""
     import math
     import attn_bwd_b200 as ab
     from attn_bwd_b200.generate import generate_input_lowmem
     torch.cuda.set_device(0)
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device="cuda")
-    stream = torch.cuda.current_stream()
+    snap = _load_snapshot(args.snapshot) if args.snapshot else None
     rows = []
     for i, (bs, sq, skv) in enumerate(SOL_SHAPES):
         data = generate_input_lowmem(bs, sq, skv, 1001 + i, device="cuda")
-        for _ in range(max(args.warmup, 3)):
-            ab.custom_kernel(data)
-        torch.cuda.synchronize()
-        ms = []
-        for _ in range(args.steps):   # as the evaluator does: flush, synchronize, events around the call
-            flush.fill_(42)
-            torch.cuda.synchronize()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            ab.custom_kernel(data)
-            e1.record()
-            torch.cuda.synchronize()
-            ms.append(e0.elapsed_time(e1))
-        us = sum(ms) / len(ms) * 1e3
+        us = _time_like_evaluator(ab.custom_kernel, data, flush, args.steps, args.warmup)
         gbs = alg_bytes(bs * KVH, sq, skv)["total"] / (us * 1e-6) / 1e9
-        rows.append({"bs": bs, "sq": sq, "skv": skv, "us": round(us, 2), "GBps": round(gbs, 1)})
+        row = {"bs": bs, "sq": sq, "skv": skv, "us": round(us, 2), "GBps": round(gbs, 1)}
+        if snap is not None:
+            with torch.no_grad():
+                us_ref = _time_like_evaluator(snap, data, flush, args.steps, args.warmup)
+                rS, rV = snap(data)
+            oS, oV = ab.custom_kernel(data)
+            torch.cuda.synchronize()
+            row["snapshot_us"] = round(us_ref, 2)
+            row["speedup"] = round(us_ref / us, 3)
+            row["outputs_match"] = bool(torch.allclose(rS.float(), oS.float(), rtol=1e-2, atol=1e-2) and
+                                        torch.allclose(rV.float(), oV.float(), rtol=1e-2, atol=1e-2))
+            del rS, rV, oS, oV
+        rows.append(row)
         del data
         torch.cuda.empty_cache()
     assert ab.poll_error() == 0
-    geo = math.exp(sum(math.log(r["us"]) for r in rows) / len(rows))
-    print(json.dumps({"sweep": "sol-execbench-16", "geomean_us": round(geo, 2), "score": round(756.0 / geo, 3),
-                      "reference_best_snapshot_geomean_us": 379.11, "shapes": rows}), flush=True)
+    geo = lambda k: math.exp(sum(math.log(r[k]) for r in rows) / len(rows))
+    line = {"sweep": "sol-execbench-16", "geomean_us": round(geo("us"), 2), "score": round(756.0 / geo("us"), 3),
+            "reference_best_snapshot_recorded_geomean_us": 379.11, "steps": args.steps, "shapes": rows}
+    if snap is not None:
+        line["snapshot"] = os.path.basename(args.snapshot)
+        line["snapshot_geomean_us_same_gpu"] = round(geo("snapshot_us"), 2)
+        line["snapshot_score_same_gpu"] = round(756.0 / geo("snapshot_us"), 3)
+        line["geomean_speedup"] = round(geo("snapshot_us") / geo("us"), 3)
+    print(json.dumps(line), flush=True)
 
 
 def run_once(args):
@@ -283,6 +352,116 @@ def run_once(args):
     print(json.dumps({"once": args.config, "ok": True}))
 
 
+class NvmlClock:
+    """SM clock read through NVML every ~2 ms on a background thread (read-only)."""
+
+    def __init__(self, device_index):
+        import threading
+        self.samples = []
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._read = lambda: pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._read()
+            self.ok = True
+        except Exception:
+            return
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                self.samples.append((time.perf_counter(), self._read()))
+                time.sleep(0.002)
+        self._t = threading.Thread(target=loop, daemon=True)
+        self._t.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def during(self, t0, t1):
+        """Median SM MHz sampled in [t0, t1], else the sample nearest the interval's middle."""
+        xs = [m for t, m in self.samples if t0 <= t <= t1]
+        if xs:
+            return statistics.median(xs)
+        if not self.samples:
+            return None
+        mid = 0.5 * (t0 + t1)
+        return min(self.samples, key=lambda s: abs(s[0] - mid))[1]
+
+
+def clock_binned(fn, launches, flush, stream, device_index, max_mhz):
+    """Each launch timed with CUDA events on its own (synchronised before and after), with
+    the SM clock NVML saw during it: launches binned by clock, and each launch's time scaled
+    to the maximum clock (us x MHz / max MHz; constant if the kernel's time is set by the
+    SM clock, the raw time constant if it is set by HBM)."""
+    clk = NvmlClock(device_index)
+    rows = []
+    for i in range(launches):
+        flush.fill_(i)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        t1 = time.perf_counter()
+        rows.append((e0.elapsed_time(e1) * 1e3, t0, t1))
+    clk.stop()
+    if not clk.ok:
+        return {"nvml": False, "us_median": round(statistics.median(r[0] for r in rows), 2)}
+    per = [(us, clk.during(t0, t1)) for us, t0, t1 in rows]
+    per = [(us, m) for us, m in per if m]
+    bins = {}
+    for us, m in per:
+        bins.setdefault(int(round(m / 15.0) * 15), []).append(us)
+    mx = max_mhz or max(m for _, m in per)
+    return {"nvml": True, "launches": len(per),
+            "us_median": round(statistics.median(us for us, _ in per), 2),
+            "us_min": round(min(us for us, _ in per), 2), "us_max": round(max(us for us, _ in per), 2),
+            "sm_mhz_median": statistics.median(m for _, m in per),
+            "us_scaled_to_max_clock_median": round(statistics.median(us * m / mx for us, m in per), 2),
+            "bins": {str(k): {"n": len(v), "us_median": round(statistics.median(v), 2)}
+                     for k, v in sorted(bins.items())}}
+
+
+def config_leg(ab, cfg, dev, steps, flush, stream, peak):
+    """Whole call, dS kernel alone and dV kernel alone on one more BASELINE config (one
+    GPU, all units), timed like the main leg; fractions of the measured HBM peak follow
+    from the algorithmic bytes and the printed us."""
+    bs, sq, skv = CONFIGS[cfg]
+    n = bs * KVH
+    data = make_shard_inputs(bs, sq, skv, 0, n, 1000 + int(cfg[1]), dev)
+    dO, P, Pd, V, M, p = data
+    step = lambda: ab.attn_bwd_shard(data, 0, n)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    call_ms = timed_loop(step, steps, flush, stream)
+    ds_ms = timed_loop(lambda: ab.ds_shard(dO, P, V, M, p, 0, n), steps, flush, stream)
+    dv_ms = timed_loop(lambda: ab.dv_shard(dO, Pd, V, 0, n), steps, flush, stream)
+    assert ab.poll_error() == 0
+    b = alg_bytes(n, sq, skv)
+    us = lambda ms: sum(ms) / len(ms) * 1e3
+    out = {"shape": [bs, sq, skv], "alg_bytes": {"call": b["total"], "ds": b["ds"], "dv": b["dv"]}}
+    for name, ms, key in (("call", call_ms, "total"), ("ds_kernel", ds_ms, "ds"), ("dv_kernel", dv_ms, "dv")):
+        t = us(ms)
+        gbs = b[key] / (t * 1e-6) / 1e9
+        out[name] = {"us": round(t, 2), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    del data, dO, P, Pd, V, M
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -297,6 +476,11 @@ def main():
                     help="one dS-kernel and one dV-kernel call on the config (for ncu), then exit")
     ap.add_argument("--sweep", choices=["sol"], default=None,
                     help="time the 16 SOL-ExecBench shapes instead of the driver line")
+    ap.add_argument("--snapshot", default=None,
+                    help="with --sweep sol: a reference submission file to time alongside (unmodified)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the c1-c3 block of the line")
+    ap.add_argument("--clock-launches", type=int, default=40,
+                    help="dS launches timed one by one against the NVML SM clock (0: skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -316,7 +500,7 @@ def main():
 
     bs, sq, skv = CONFIGS[args.config]
     n_units = bs * KVH
-    u0, u1 = shard_range(n_units, rank, world)
+    u0, u1 = shard_range(n_units, rank, world, sq, skv)
     dev = torch.device("cuda", local)
     data = make_shard_inputs(bs, sq, skv, u0, u1, 1000 + int(args.config[1]), dev)
     dO, P, Pd, V, M, p = data
@@ -412,6 +596,28 @@ def main():
         gather_ms = max_over_ranks(g0.elapsed_time(g1), world)
         del out, s_, v_
 
+    # ---- dS launches one by one against the SM clock (rank 0 of a 1-GPU run)
+    ds_clock = None
+    if world == 1 and args.clock_launches > 0:
+        try:
+            mx = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("sm_max_mhz", 0))
+        except Exception:
+            mx = 0.0
+        ds_clock = clock_binned(ds_only, args.clock_launches, flush, stream, local, mx)
+
+    # ---- the other BASELINE configs on one GPU (c4 inputs freed first)
+    configs = None
+    if world == 1 and args.config == "c4" and not args.no_configs:
+        del data, dO, P, Pd, V, M, host, host_data, work, dS_h, dV_h
+        torch.cuda.empty_cache()
+        configs = {}
+        for cfg in ("c1", "c2", "c3"):
+            configs[cfg] = config_leg(ab, cfg, dev, args.steps, flush, stream, peak)
+        configs["c4"] = {"shape": [bs, sq, skv], "call": {"us": round(t_step / args.steps * 1e6, 2),
+                                                           "frac": round(value / peak, 4)},
+                         "ds_kernel": {"us": round(t_ds * 1e6, 2), "frac": round(ds_gbs / peak, 4)},
+                         "dv_kernel": {"us": round(t_dv * 1e6, 2), "frac": round(dv_gbs / peak, 4)}}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, n, secs = cpu_sample(args.config)
@@ -446,7 +652,12 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e / args.e2e_steps * 1e3, 2)},
             "gpu_launches": 2 * args.steps,
             "gather_to_rank0_ms": None if gather_ms is None else round(gather_ms, 3),
+            "gather_to_rank0_GBps": None if gather_ms is None else round(
+                (alg_bytes(n_units, sq, skv)["E"] * 2 + n_units * skv * D * 2) * (world - 1) / world
+                / (gather_ms * 1e-3) / 1e9, 1),
             "clocks": clocks,
+            "ds_kernel_vs_clock": ds_clock,
+            "configs": configs,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

@@ -16,8 +16,18 @@
  *   grad_value_states     dV   [bs, 8, seq_kv, 128]      bf16 (output)
  *
  * All pointers are device pointers to contiguous tensors, 16-byte aligned (the host-buffer
- * calls also take host pointers, named *_h).  Every call is asynchronous on `stream` and allocates nothing.  Returns 0 on
- * success or one of the ATTN_BWD_E* codes (nothing is launched on error).
+ * calls also take host pointers, named *_h).  Every call is asynchronous on `stream` and
+ * returns 0 on success or one of the ATTN_BWD_E* codes (nothing is launched on error).
+ *
+ * Memory and resources: no call allocates device memory for tensors; outputs and (for the
+ * host-buffer call) device buffers are the caller's.  The library does create, lazily and
+ * per device, resources that live until attn_bwd_b200_release() or process exit:
+ *   - on the first full call: one side stream (dV runs there next to dS) and two events;
+ *   - on the second full call with a given argument list: an instantiated CUDA graph of
+ *     that call's launches (a 16-entry LRU per device; a graph holds a little device
+ *     memory for its nodes) and one private capture stream;
+ *   - on the first host-buffer call: two copy streams and 130 events.
+ * A device-side error word (see attn_bwd_b200_poll_error) is a static __device__ variable.
  */
 #ifndef ATTN_BWD_B200_H
 #define ATTN_BWD_B200_H
@@ -122,6 +132,36 @@ const char* attn_bwd_b200_strerror(int code);
 
 /* ABI version of this library (major*100 + minor). */
 int attn_bwd_b200_version(void);
+
+/* Frees the lazily created per-device resources listed at the top of this file (side,
+ * capture and copy streams, events, cached launch graphs) of the CURRENT device, after
+ * synchronising it.  Later calls re-create what they need.  No reference counterpart. */
+int attn_bwd_b200_release(void);
+
+/* Measurement and test options (no reference counterpart).  Every option defaults to -1,
+ * "automatic": the library then picks the kernel form measured fastest for the shape,
+ * which is what production callers should use.  An option forces one choice instead, for
+ * A/B measurements and for tests that must reach every kernel form.  Options are
+ * process-wide, take effect from the next call, and invalidate cached launch graphs.
+ * Forcing a form never changes the math, only which kernel computes it (the compact dS
+ * form rounds the masked dP~ to bf16 before the softmax step, as noted in its kernel).
+ * Returns ATTN_BWD_EINVAL for an unknown option. */
+enum {
+  ATTN_BWD_OPT_DS_MODE = 0,      /* 0 recompute, 1 resident, 2 TMEM-held P, 3 compact (where the shape allows) */
+  ATTN_BWD_OPT_ROW_KIND = 1,     /* 1 per-row re-aligned (rows not 16-byte multiples), 2 class tiles (any rows) */
+  ATTN_BWD_OPT_DS_CLUSTER = 2,   /* n CTAs per row (1..8) for the resident form, when the row fits */
+  ATTN_BWD_OPT_L2_PREFETCH = 3,  /* 0/1: L2 prefetch of a CTA's next unit during pass 2 (aligned rows) */
+  ATTN_BWD_OPT_L2_HINT = 4,      /* 0 off, 1 aligned rows (default), 2 also class-tile rows */
+  ATTN_BWD_OPT_SPLIT = 5,        /* 0 plain / 1 split form of the dS + dV overlap */
+  ATTN_BWD_OPT_DV_SMS = 6,       /* SMs given to dV in the split form */
+  ATTN_BWD_OPT_SIDE_STREAM = 7,  /* 0: dS and dV back to back on the caller's stream */
+  ATTN_BWD_OPT_GRAPH = 8,        /* 0: never replay full calls from cached CUDA graphs */
+  ATTN_BWD_OPT_MAP_CACHE = 9,    /* 0: encode every TMA descriptor on every call */
+  ATTN_BWD_OPT_COUNT = 10
+};
+int attn_bwd_b200_set_option(int option, int value);
+/* Current value of an option (-1 = automatic), or -2 for an unknown option. */
+int attn_bwd_b200_get_option(int option);
 
 #ifdef __cplusplus
 }

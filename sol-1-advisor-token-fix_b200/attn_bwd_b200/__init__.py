@@ -19,7 +19,8 @@ NUM_GROUPS = NUM_ATTENTION_HEADS // NUM_KEY_VALUE_HEADS
 HEAD_DIM = 128
 
 __all__ = ["custom_kernel", "attn_bwd", "attn_bwd_shard", "attn_bwd_host", "ds_shard", "dv_shard", "run",
-           "AttnBwdError", "poll_error", "NUM_ATTENTION_HEADS", "NUM_KEY_VALUE_HEADS", "HEAD_DIM"]
+           "AttnBwdError", "poll_error", "release", "options", "NUM_ATTENTION_HEADS", "NUM_KEY_VALUE_HEADS",
+           "HEAD_DIM"]
 
 
 def _ptr(t):
@@ -172,6 +173,10 @@ def attn_bwd_host(data, unit_begin=None, unit_end=None, device=None, work=None, 
                   _ptr(dS_h), _ptr(dV_h), *(_ptr(w) for w in work), int(chunks), _stream())
         if synchronize:
             torch.cuda.current_stream().synchronize()
+            # the stream is idle: a kernel wait that gave up would otherwise go unnoticed
+            rc = _lib.load().attn_bwd_b200_poll_error()
+            if rc:
+                raise AttnBwdError("attn_bwd_b200_host_shard", _lib.EKERNEL if rc > 0xFF else rc)
     return dS_h, dV_h
 
 
@@ -318,3 +323,33 @@ def dv_shard(dO, Pd, V, unit_begin, unit_end, out=None):
 def poll_error():
     """Synchronise and return (and clear) the code of a kernel wait that gave up; 0 if none."""
     return _lib.load().attn_bwd_b200_poll_error()
+
+
+def release():
+    """Synchronise the current device and free the library's lazily created streams,
+    events and cached launch graphs on it (later calls re-create them)."""
+    _lib.call("attn_bwd_b200_release")
+
+
+class options:
+    """Context manager forcing measurement / test options of the library for its body,
+    e.g. ``with options(ds_mode=3): ...`` (names and values: ATTN_BWD_OPT_* in
+    include/attn_bwd_b200.h).  Process-wide; the previous values are restored on exit."""
+
+    def __init__(self, **opts):
+        for k in opts:
+            if k not in _lib.OPTIONS:
+                raise ValueError(f"unknown option {k!r}; known: {sorted(_lib.OPTIONS)}")
+        self.opts = opts
+        self.saved = {}
+
+    def __enter__(self):
+        for k, v in self.opts.items():
+            self.saved[k] = _lib.get_option(k)
+            _lib.set_option(k, v)
+        return self
+
+    def __exit__(self, *exc):
+        for k, v in self.saved.items():
+            _lib.set_option(k, v)
+        return False

@@ -27,7 +27,14 @@ SIGNATURES = {
     "attn_bwd_b200_selftest_wait_timeout": (_I, [_I, _VP]),
     "attn_bwd_b200_strerror": (ctypes.c_char_p, [_I]),
     "attn_bwd_b200_version": (_I, []),
+    "attn_bwd_b200_release": (_I, []),
+    "attn_bwd_b200_set_option": (_I, [_I, _I]),
+    "attn_bwd_b200_get_option": (_I, [_I]),
 }
+
+# Measurement / test options (ATTN_BWD_OPT_* in include/attn_bwd_b200.h); -1 = automatic.
+OPTIONS = {"ds_mode": 0, "row_kind": 1, "ds_cluster": 2, "l2_prefetch": 3, "l2_hint": 4, "split": 5,
+           "dv_sms": 6, "side_stream": 7, "graph": 8, "map_cache": 9}
 
 _lib = None
 
@@ -64,6 +71,15 @@ def fast_fn():
 
 def strerror(code):
     return load().attn_bwd_b200_strerror(int(code)).decode()
+
+
+def set_option(name, value):
+    """Sets one measurement / test option (process-wide; -1 restores the automatic choice)."""
+    call("attn_bwd_b200_set_option", OPTIONS[name], int(value))
+
+
+def get_option(name):
+    return load().attn_bwd_b200_get_option(OPTIONS[name])
 
 
 def call(name, *args):

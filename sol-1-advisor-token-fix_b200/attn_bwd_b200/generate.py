@@ -7,10 +7,13 @@ reference draws on a CUDA generator; here the generator's device is a
 parameter.  With ``device="cpu"`` the same seed gives bit-identical inputs on
 every machine running this torch build, which is what the golden fixtures and
 CPU-vs-GPU parity tests rely on.
+
+The module imports nothing from its package, so a CPU-only user (the benchmark's
+reference arm) can load it by file path without loading the CUDA library.
 """
 import torch
 
-from . import NUM_ATTENTION_HEADS as H, NUM_KEY_VALUE_HEADS as KVH, HEAD_DIM as D
+H, KVH, D = 80, 8, 128   # query heads, KV heads, head_dim (starting_point.py:22-24)
 
 
 def generate_input(batch_size, seq_len_q, seq_len_kv, seed, dropout_p=0.1, device="cpu",

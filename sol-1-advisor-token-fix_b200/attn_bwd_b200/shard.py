@@ -14,11 +14,27 @@ import torch.distributed as dist
 KVH, G, H, D = 8, 10, 80, 128
 
 
-def unit_range(n_units, rank, world):
-    """Contiguous, balanced split of [0, n_units) (sizes differ by at most 1)."""
+def unit_step(sq, skv):
+    """Smallest g in {1, 2, 4, 8} for which g units (10·g heads of sq·skv elements) are a
+    multiple of 16 elements: shard boundaries on multiples of g keep every slice of P /
+    P_drop / mask / dS 16-byte aligned and keep the rows' alignment classes (the same rule
+    as the C library's host-buffer pipeline)."""
+    for g in (1, 2, 4):
+        if (G * g * sq * skv) % 16 == 0:
+            return g
+    return 8
+
+
+def unit_range(n_units, rank, world, sq=None, skv=None):
+    """Contiguous, balanced split of [0, n_units).  Without (sq, skv) sizes differ by at
+    most 1; with them, boundaries fall on multiples of unit_step(sq, skv), so that every
+    rank's slices start 16-byte aligned and need no copy (sizes then differ by at most one
+    step)."""
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} / world {world}")
-    return n_units * rank // world, n_units * (rank + 1) // world
+    g = 1 if sq is None or skv is None else unit_step(sq, skv)
+    steps = (n_units + g - 1) // g
+    return min(steps * rank // world * g, n_units), min(steps * (rank + 1) // world * g, n_units)
 
 
 def head_slice(u0, u1):
@@ -36,26 +52,42 @@ def shard_inputs(data, u0, u1):
     return dO, flat(P), flat(Pd), V, flat(M), p
 
 
-def gather_to_rank0(dS_shard, dV_shard, bs, sq, skv, group=None):
+def gather_to_rank0(dS_shard, dV_shard, bs, sq, skv, group=None, out=None, aligned=True):
     """Collects every rank's (dS_shard, dV_shard) into full [bs,80,sq,skv] and
-    [bs,8,skv,128] tensors on rank 0 (returns None elsewhere).  Shards must be
-    the unit_range() split of bs*8 units over the group."""
+    [bs,8,skv,128] tensors on rank 0 (returns None elsewhere).  Shards must be the
+    unit_range() split of bs*8 units over the group (aligned=True: the split with
+    (sq, skv), as the multi-GPU path uses; False: the plain split).  ``out`` optionally
+    supplies rank 0's (dS, dV) destination tensors.
+
+    All transfers are posted as one batch of point-to-point operations, so every peer
+    streams into rank 0 at the same time (NCCL runs them concurrently over NVLink)."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     n_units = bs * KVH
+    rng = (lambda r: unit_range(n_units, r, world, sq, skv)) if aligned else (lambda r: unit_range(n_units, r, world))
     if rank != 0:
-        dist.send(dS_shard.contiguous(), dst=0, group=group)
-        dist.send(dV_shard.contiguous(), dst=0, group=group)
+        ops = [dist.P2POp(dist.isend, dS_shard.contiguous(), 0, group),
+               dist.P2POp(dist.isend, dV_shard.contiguous(), 0, group)]
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
         return None
-    dS = torch.empty(bs * H, sq, skv, dtype=dS_shard.dtype, device=dS_shard.device)
-    dV = torch.empty(bs * KVH, skv, D, dtype=dV_shard.dtype, device=dV_shard.device)
-    for r in range(world):
-        u0, u1 = unit_range(n_units, r, world)
+    if out is None:
+        dS = torch.empty(bs * H, sq, skv, dtype=dS_shard.dtype, device=dS_shard.device)
+        dV = torch.empty(bs * KVH, skv, D, dtype=dV_shard.dtype, device=dV_shard.device)
+    else:
+        dS = out[0].view(bs * H, sq, skv)
+        dV = out[1].view(bs * KVH, skv, D)
+    ops = []
+    for r in range(1, world):
+        u0, u1 = rng(r)
         h0, h1 = head_slice(u0, u1)
-        if r == 0:
-            dS[h0:h1].copy_(dS_shard)
-            dV[u0:u1].copy_(dV_shard)
-        else:
-            dist.recv(dS[h0:h1], src=r, group=group)
-            dist.recv(dV[u0:u1], src=r, group=group)
+        ops.append(dist.P2POp(dist.irecv, dS[h0:h1], r, group))
+        ops.append(dist.P2POp(dist.irecv, dV[u0:u1], r, group))
+    works = dist.batch_isend_irecv(ops) if ops else []
+    u0, u1 = rng(0)
+    h0, h1 = head_slice(u0, u1)
+    dS[h0:h1].copy_(dS_shard)
+    dV[u0:u1].copy_(dV_shard)
+    for w in works:
+        w.wait()
     return dS.view(bs, H, sq, skv), dV.view(bs, KVH, skv, D)

@@ -3,6 +3,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/attn_bwd_b200.h"
@@ -53,6 +54,19 @@ struct DeviceState {
 };
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
+
+// Measurement / test options (attn_bwd_b200_set_option).  Process-wide; every call reads
+// them when it chooses its kernels; the generation counter is part of the launch-graph key,
+// so a change never replays a graph recorded under other options.
+constexpr int kNumOptions = ATTN_BWD_OPT_COUNT;
+std::atomic<int> g_opt[kNumOptions];
+std::atomic<unsigned> g_opt_gen{0};
+struct OptDefaults {
+  OptDefaults() {
+    for (int i = 0; i < kNumOptions; ++i) g_opt[i].store(-1);
+  }
+} g_opt_defaults;
+inline int opt(int k) { return g_opt[k].load(std::memory_order_relaxed); }
 EncodeTiledFn g_encode = nullptr;
 
 bool set_ds_smem() {
@@ -115,7 +129,7 @@ bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* pt
 
 // Encoded descriptors, direct-mapped by a hash of every encode argument (a descriptor
 // depends on nothing else), so repeated calls on the same tensors skip the driver call.
-// ATTN_BWD_NO_MAP_CACHE=1 encodes every time.
+// Option ATTN_BWD_OPT_MAP_CACHE = 0 encodes every time.
 struct MapEntry {
   uint64_t key[16];
   bool valid;
@@ -127,7 +141,7 @@ std::mutex g_map_mu;
 
 bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
               const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
-  static const bool cache_on = std::getenv("ATTN_BWD_NO_MAP_CACHE") == nullptr;
+  const bool cache_on = opt(ATTN_BWD_OPT_MAP_CACHE) != 0;
   if (!cache_on || rank > 5) return encode_map(m, dt, rank, ptr, dims, strides, box, sw);
   uint64_t key[16] = {};
   key[0] = (uint64_t)dt | ((uint64_t)rank << 8) | ((uint64_t)sw << 16);
@@ -189,15 +203,9 @@ int check_shape(const Shape& s) {
 //     dedicated ones: c1 100 vs 120 us), kCompact for 9-10 chunks (one CTA instead of a
 //     cluster), kResident on clusters beyond that;
 //   then kResident on clusters up to 8 x 512 columns, then kRecompute.
-// ATTN_BWD_DS_MODE = 0/1/2 forces recompute / resident / TMEM-P where the shape
-// allows it (for measurements), read once.
-int forced_ds_mode() {
-  static const int v = [] {
-    const char* e = std::getenv("ATTN_BWD_DS_MODE");
-    return e ? std::atoi(e) : -1;
-  }();
-  return v;
-}
+// Option ATTN_BWD_OPT_DS_MODE = 0/1/2/3 forces recompute / resident / TMEM-P / compact
+// where the shape allows it (measurements and tests).
+int forced_ds_mode() { return opt(ATTN_BWD_OPT_DS_MODE); }
 
 // seq_kv rows of P / mask / dS must be 16-byte multiples for the TMA path.
 inline bool tma_rows_ok(int skv) { return (skv % 16) == 0; }
@@ -218,10 +226,10 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   // per-row re-aligning kernel.  Measured on B200 (dS us, class / per-row; slot ratio):
   // c2 243 / 339 (0.80), 32x691x773 2264 / 3730 (0.93), 8x373x449 212 / 240 (1.07),
   // 4x211x293 76 / 62 (1.20).
-  // ATTN_BWD_RAGGED_ROWS=1 / ATTN_BWD_CLASS_ROWS=1 force one of the two (the latter also
-  // for aligned rows, as a measurement of the class layout alone).
-  static const bool force_ragged = std::getenv("ATTN_BWD_RAGGED_ROWS") != nullptr;
-  static const bool force_class = std::getenv("ATTN_BWD_CLASS_ROWS") != nullptr;
+  // Option ATTN_BWD_OPT_ROW_KIND = 1 (per-row) / 2 (class tiles) forces one of the two (the
+  // latter also for aligned rows, as a measurement of the class layout alone).
+  const bool force_ragged = opt(ATTN_BWD_OPT_ROW_KIND) == 1;
+  const bool force_class = opt(ATTN_BWD_OPT_ROW_KIND) == 2;
   const bool rag = !tma_rows_ok(s.skv);
   int rk = ds::kRowsAligned;
   if (rag || force_class) {
@@ -317,8 +325,8 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   } else if (prm.nchunks <= 8 * ds::TSLOTS && forced != ds::kRecompute) {
     mode = ds::kResident;
     split(ds::TSLOTS);
-    // measurement knob: ATTN_BWD_DS_CLUSTER = n forces n CTAs per row (1..8) when it fits
-    static const int forced_cs = std::getenv("ATTN_BWD_DS_CLUSTER") ? std::atoi(std::getenv("ATTN_BWD_DS_CLUSTER")) : 0;
+    // option ATTN_BWD_OPT_DS_CLUSTER = n forces n CTAs per row (1..8) when it fits
+    const int forced_cs = opt(ATTN_BWD_OPT_DS_CLUSTER);
     if (forced_cs >= 1 && forced_cs <= 8 && (prm.nchunks + forced_cs - 1) / forced_cs <= ds::TSLOTS &&
         forced_cs <= prm.nchunks) {
       prm.cs = forced_cs;
@@ -336,14 +344,14 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   // over the SOL-ExecBench shapes and c1-c4, it helps rows of up to 6 chunks held by one
   // CTA (c1 dS 97 -> 91 us, 64x128x128 161 -> 155 us) and hurts longer rows (c4 dS
   // 2010 -> 2096 us, 1x4096x4096 +5 %), where the extra L2 footprint evicts pass-2 data.
-  // ATTN_BWD_L2PF=0/1 forces it off / on (measurements).
-  static const int l2pf_env = std::getenv("ATTN_BWD_L2PF") ? std::atoi(std::getenv("ATTN_BWD_L2PF")) : -1;
+  // Option ATTN_BWD_OPT_L2_PREFETCH = 0/1 forces it off / on (measurements).
+  const int l2pf_env = opt(ATTN_BWD_OPT_L2_PREFETCH);
   prm.l2pf = l2pf_env >= 0 ? l2pf_env : (prm.cs == 1 && prm.nchunks <= 6 ? 1 : 0);
   // L2 eviction hints on the aligned path (pass-1 P / mask kept for pass 2, pass-2 reloads
   // and dS stores evicted first): measured on B200, c3 dS 1279 -> 1245 us, c1 96 -> 91 us,
-  // c4 unchanged.  ATTN_BWD_L2HINT=0 turns them off (measurements).
-  static const int l2hint_env = std::getenv("ATTN_BWD_L2HINT") ? std::atoi(std::getenv("ATTN_BWD_L2HINT")) : 1;
-  // class rows: ATTN_BWD_L2HINT=2 (measurement) also applies them there
+  // c4 unchanged.  Option ATTN_BWD_OPT_L2_HINT = 0 turns them off (measurements).
+  const int l2hint_env = opt(ATTN_BWD_OPT_L2_HINT) < 0 ? 1 : opt(ATTN_BWD_OPT_L2_HINT);
+  // class rows: option value 2 (measurement) also applies them there
   prm.l2hint = rk == ds::kRowsClass ? (l2hint_env == 2 ? 1 : 0) : (l2hint_env != 0 ? 1 : 0);
   prm.scale = p > 0.f ? 1.0f / (1.0f - p) : 1.0f;
   prm.err = st.err;
@@ -506,13 +514,13 @@ int enqueue_full_locked(DeviceState* st, const Shape& s, const void* dO, const v
   //   plain  (larger): dS is launched first with the full grid and dV's CTAs take over
   //          SMs as dS CTAs finish, filling the dS kernel's tail (1x4096x4096: 2306 us
   //          back to back -> 1979 us).
-  // ATTN_BWD_NO_SIDE_STREAM=1 runs them back to back on one stream.
+  // Option ATTN_BWD_OPT_SIDE_STREAM = 0 runs them back to back on one stream.
   const int dvc = dv_ctas(*st, s);
   const bool rag_rows = !tma_rows_ok(s.skv);
   const double elems = (double)s.n_units() * kGroups * s.sq * s.skv;
   const bool small = elems <= (rag_rows ? 64e6 : 256e6);
   const int dv_share = (st->sm_count * (rag_rows ? 48 : 32) + 147) / 148;
-  static const bool side_on = std::getenv("ATTN_BWD_NO_SIDE_STREAM") == nullptr;
+  const bool side_on = opt(ATTN_BWD_OPT_SIDE_STREAM) != 0;
   if (side_on && dvc > 0) {
     if (!st->side) {
       if (cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking) != cudaSuccess ||
@@ -520,10 +528,10 @@ int enqueue_full_locked(DeviceState* st, const Shape& s, const void* dO, const v
           cudaEventCreateWithFlags(&st->join, cudaEventDisableTiming) != cudaSuccess)
         return ATTN_BWD_ECUDA;
     }
-    // measurement knobs: ATTN_BWD_SPLIT=0/1 forces the plain / split form, ATTN_BWD_DV_SMS=n
-    // sets the dV share of the split form
-    static const int force_split = std::getenv("ATTN_BWD_SPLIT") ? std::atoi(std::getenv("ATTN_BWD_SPLIT")) : -1;
-    static const int dv_sms = std::getenv("ATTN_BWD_DV_SMS") ? std::atoi(std::getenv("ATTN_BWD_DV_SMS")) : 0;
+    // options ATTN_BWD_OPT_SPLIT = 0/1 force the plain / split form, ATTN_BWD_OPT_DV_SMS = n
+    // sets the dV share of the split form (measurements)
+    const int force_split = opt(ATTN_BWD_OPT_SPLIT);
+    const int dv_sms = opt(ATTN_BWD_OPT_DV_SMS);
     int dv_grid = dv_sms > 0 ? dv_sms : dv_share;
     if (dv_grid > dvc) dv_grid = dvc;
     const int budget = st->sm_count - dv_grid;
@@ -560,10 +568,10 @@ int enqueue_full(DeviceState* st, const Shape& s, const void* dO, const void* P,
 // a graph, later ones replay it with one cudaGraphLaunch on the caller's stream, which
 // removes most of the host-side launch cost for repeated calls on the same tensors.
 // The replay depends only on the argument list (pointers, shape, dropout, stream): input
-// contents may change freely between calls.  ATTN_BWD_NO_GRAPH=1 turns this off.
+// contents may change freely between calls.  Option ATTN_BWD_OPT_GRAPH = 0 turns this off.
 int run_full(DeviceState* st, const Shape& s, const void* dO, const void* P, const void* Pd, const void* V,
              const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs) {
-  static const bool graphs_on = std::getenv("ATTN_BWD_NO_GRAPH") == nullptr;
+  const bool graphs_on = opt(ATTN_BWD_OPT_GRAPH) != 0;
   if (!graphs_on) return enqueue_full(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
   // a caller that is itself capturing this stream gets the plain launches in its graph
   cudaStreamCaptureStatus cap_status = cudaStreamCaptureStatusNone;
@@ -571,9 +579,10 @@ int run_full(DeviceState* st, const Shape& s, const void* dO, const void* P, con
   if (cap_status != cudaStreamCaptureStatusNone) return enqueue_full(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
   uint32_t pbits;
   std::memcpy(&pbits, &p, 4);
+  // the options generation rides in the dropout word: a graph never outlives its options
   const uint64_t key[14] = {(uint64_t)dO, (uint64_t)P, (uint64_t)Pd, (uint64_t)V, (uint64_t)M, (uint64_t)dS,
-                            (uint64_t)dV, pbits, (uint64_t)s.bs, (uint64_t)s.sq, (uint64_t)s.skv, (uint64_t)s.u0,
-                            (uint64_t)s.u1, (uint64_t)cs};
+                            (uint64_t)dV, pbits | ((uint64_t)g_opt_gen.load() << 32), (uint64_t)s.bs,
+                            (uint64_t)s.sq, (uint64_t)s.skv, (uint64_t)s.u0, (uint64_t)s.u1, (uint64_t)cs};
   std::lock_guard<std::mutex> lk(st->side_mu);
   DeviceState::GraphEntry* hit = nullptr;
   DeviceState::GraphEntry* victim = &st->graphs[0];
@@ -840,7 +849,54 @@ const char* attn_bwd_b200_strerror(int code) {
   }
 }
 
-int attn_bwd_b200_version(void) { return 101; }
+int attn_bwd_b200_version(void) { return 102; }
+
+int attn_bwd_b200_set_option(int option, int value) {
+  if (option < 0 || option >= kNumOptions) return ATTN_BWD_EINVAL;
+  g_opt[option].store(value);
+  g_opt_gen.fetch_add(1);
+  return ATTN_BWD_OK;
+}
+
+int attn_bwd_b200_get_option(int option) {
+  if (option < 0 || option >= kNumOptions) return -2;
+  return g_opt[option].load();
+}
+
+int attn_bwd_b200_release(void) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) return ATTN_BWD_ECUDA;
+  std::lock_guard<std::mutex> lk_side(st->side_mu);
+  std::lock_guard<std::mutex> lk_host(st->host_mu);
+  bool ok = true;
+  for (auto& g : st->graphs) {
+    if (g.state == 2 && g.exec) ok &= cudaGraphExecDestroy(g.exec) == cudaSuccess;
+    g = DeviceState::GraphEntry{};
+  }
+  auto drop_stream = [&](cudaStream_t& s) {
+    if (s) ok &= cudaStreamDestroy(s) == cudaSuccess;
+    s = nullptr;
+  };
+  auto drop_event = [&](cudaEvent_t& e) {
+    if (e) ok &= cudaEventDestroy(e) == cudaSuccess;
+    e = nullptr;
+  };
+  drop_stream(st->side);
+  drop_stream(st->cap);
+  drop_stream(st->h2d);
+  drop_stream(st->d2h);
+  drop_event(st->fork);
+  drop_event(st->join);
+  drop_event(st->h_fork);
+  drop_event(st->h_join);
+  for (int k = 0; k < kMaxHostChunks; ++k) {
+    drop_event(st->in_done[k]);
+    drop_event(st->comp_done[k]);
+  }
+  return ok ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
+}
 
 #ifdef ATTN_BWD_WAIT_STATS
 // Diagnostics builds only (not part of the ABI): copies and clears the per-site wait cycles.

@@ -553,9 +553,10 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
             const int col0 = c * BN - cu.s;   // window start column (a multiple of 8 elements from the row start's class offset)
             if (!cu.fallback) {
               // per sub-class: one P box (64 rows x 128 B, SW128) and one mask box (64 rows x 80 B)
-              if (lane == 0) mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
+              const bool want_m = !(CP && pass == 1);   // kCompact's pass 2 needs P alone
+              if (lane == 0) mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + (want_m ? C::M_BYTES : 0));
               __syncwarp();
-              if (lane < 4) {
+              if (lane < (want_m ? 4 : 2)) {
                 const int h = lane & 1;
                 const int y = int((cu.g0 + (h ? cu.rho[1] : cu.rho[0])) >> 4);
                 const int xe = (h ? cu.cls[1] : cu.cls[0]) * skv + col0;   // element offset inside the 16-row group
@@ -599,15 +600,18 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
             }
           } else if constexpr (!RAG) {
             if (lane == 0) {
-              mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + C::M_BYTES);
+              // kCompact keeps the MASKED dP~, so its pass 2 needs P alone
+              const bool want_m = !(CP && pass == 1);
+              mbar_arrive_expect_tx(&PM_full[ps], C::P_BYTES + (want_m ? C::M_BYTES : 0));
               if (prm.l2hint) {
                 // pass 1's tiles are read again by pass 2 (keep them); pass 2 is their last use
                 const uint64_t pol = (pass == 0 && !TP) ? policy_evict_last() : policy_evict_first();
                 tma_load_3d_hint(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl, pol);
-                tma_load_3d_hint(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl, pol);
+                if (want_m)
+                  tma_load_3d_hint(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl, pol);
               } else {
                 tma_load_3d(smem + C::OFF_P + ps * C::P_BYTES, &tm_P, &PM_full[ps], c * BN, mb * BM, bhl);
-                tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
+                if (want_m) tma_load_3d(smem + C::OFF_M + ps * C::M_BYTES, &tm_M, &PM_full[ps], c * BN, mb * BM, bhl);
               }
               // pass 2 re-reads this unit from L2, which leaves HBM idle for this CTA: pull
               // the same chunk of the CTA's next unit into L2 meanwhile, so that unit's
@@ -1008,12 +1012,24 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         const unsigned long long el = row_el + (unsigned long long)c * BN;
         const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
         uint32_t pw[8], mw[4], mx[4];
-        if constexpr (CLS)
-          load_row_cls(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, mo, pw, mw);
-        else
-          load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, uint32_t(el * 2) & 15u,
-                        uint32_t(el) & 15u, pw, mw);
-        expand_mask(mw, use_mask, mx);
+        if constexpr (CP && !RAG) {
+          // the compact store holds the masked dP~ and pass 2 loaded no mask: P only
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint4 t = lds128(p_stage + row * 128 + (((cg * 2 + i) ^ (row & 7)) << 4));
+            pw[4 * i] = t.x; pw[4 * i + 1] = t.y; pw[4 * i + 2] = t.z; pw[4 * i + 3] = t.w;
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mx[i] = 0xFFFFFFFFu;
+          (void)mw;
+        } else {
+          if constexpr (CLS)
+            load_row_cls(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, mo, pw, mw);
+          else
+            load_row<RAG>(p_stage, smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row, cg, uint32_t(el * 2) & 15u,
+                          uint32_t(el) & 15u, pw, mw);
+          expand_mask(mw, use_mask, mx);
+        }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float t0 = __uint_as_float(v[2 * k] & mask_at(mx, 2 * k));

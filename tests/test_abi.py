@@ -85,3 +85,18 @@ def test_host_call_argument_errors_without_gpu():
         ab.attn_bwd_host(data, 0, 9)
     with pytest.raises(TypeError):
         ab.attn_bwd_host((None,) + tuple(data[1:]))
+
+
+def test_options_set_get_restore_without_gpu():
+    """The measurement / test options are plain host state: settable without a device,
+    restored by the context manager, unknown names and indices rejected."""
+    import attn_bwd_b200 as ab
+    lib = _lib.load()
+    assert _lib.get_option("ds_mode") == -1
+    with ab.options(ds_mode=0, graph=0):
+        assert _lib.get_option("ds_mode") == 0 and _lib.get_option("graph") == 0
+    assert _lib.get_option("ds_mode") == -1 and _lib.get_option("graph") == -1
+    with pytest.raises(ValueError):
+        ab.options(no_such_option=1)
+    assert lib.attn_bwd_b200_set_option(99, 1) == _lib.EINVAL
+    assert lib.attn_bwd_b200_get_option(99) == -2

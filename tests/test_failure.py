@@ -15,7 +15,7 @@ from attn_bwd_b200.shard import gather_to_rank0
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
-    bs, sq, skv = 1, 2, 16          # 8 units, 4 per rank
+    bs, sq, skv = 1, 2, 16          # 8 units, 4 per rank (unit_step 1)
     dS = torch.zeros(40, sq, skv, dtype=torch.bfloat16)
     dV = torch.zeros(4, skv, 128, dtype=torch.bfloat16)
     if rank == 1:

@@ -40,6 +40,24 @@ def test_unit_range_partition():
             assert max(sizes) - min(sizes) <= 1
 
 
+def test_aligned_unit_range_keeps_slices_16_byte_aligned():
+    """With (sq, skv) the split falls on unit_step boundaries: every rank's first head of
+    P / mask starts on a 16-element boundary, and the ranges still tile [0, n)."""
+    from attn_bwd_b200.shard import unit_step
+    for sq, skv in ((640, 640), (301, 467), (7, 29), (1, 1), (3, 5)):
+        g = unit_step(sq, skv)
+        assert (10 * g * sq * skv) % 16 == 0
+        for n in (8, 16, 96, 384):
+            for w in (1, 2, 3, 4, 8):
+                rs = [unit_range(n, r, w, sq, skv) for r in range(w)]
+                assert rs[0][0] == 0 and rs[-1][1] == n
+                assert all(a[1] == b[0] for a, b in zip(rs, rs[1:]))
+                for a, _ in rs:
+                    assert (a * 10 * sq * skv) % 16 == 0
+                sizes = [b - a for a, b in rs]
+                assert max(sizes) - min(sizes) <= g
+
+
 def test_shard_inputs_are_views_of_the_units_heads():
     data = generate_input(2, 4, 16, 3)
     dO, P, Pd, V, M, p = shard_inputs(data, 3, 11)
@@ -51,9 +69,9 @@ def test_shard_inputs_are_views_of_the_units_heads():
 def _worker(rank, world, port, result_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    bs, sq, skv = 2, 8, 24
+    bs, sq, skv = 2, 8, 23          # ragged rows: the aligned split has 2-unit steps
     data = generate_input(bs, sq, skv, 5)
-    u0, u1 = unit_range(bs * 8, rank, world)
+    u0, u1 = unit_range(bs * 8, rank, world, sq, skv)
     # each rank computes its units with the CPU oracle (stands in for the GPU call)
     res = attn_bwd_units(data, range(u0, u1))
     dS = torch.cat([res[u][0] for u in range(u0, u1)])

@@ -176,46 +176,41 @@ def test_bounded_wait_reports_and_recovers(cuda):
     _check_full(generate_input(1, 16, 64, 8), cuda)
 
 
-_MODE_SCRIPT = r"""
-import sys, torch
-sys.path[:0] = [{root!r}, {pkg!r}]
-import attn_bwd_b200 as ab
-from attn_bwd_b200.generate import generate_input
-from oracle.attn_bwd_oracle import attn_bwd_reference
-bad = []
-for shape in {shapes!r}:
-    data = generate_input(*shape, seed=31)
-    dS, dV = ab.custom_kernel(tuple(t.cuda() if isinstance(t, torch.Tensor) else t for t in data))
-    torch.cuda.synchronize()
-    rS, rV = attn_bwd_reference(data)
-    ok = (torch.allclose(rS.float(), dS.float().cpu(), rtol=1e-2, atol=1e-2) and
-          torch.allclose(rV.float(), dV.float().cpu(), rtol=1e-2, atol=1e-2) and ab.poll_error() == 0)
-    if not ok:
-        bad.append(shape)
-print("BAD" if bad else "OK", bad)
-"""
-
-
 @pytest.mark.parametrize("rows", ["class", "ragged"])
-@pytest.mark.parametrize("mode", ["0", "1", "2", "3"])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
 def test_every_ds_mode(mode, rows, cuda):
     """Each pass-2 mode of the dS kernel (recompute / resident / TMEM-held P / compact), forced
-    through ATTN_BWD_DS_MODE where the shape allows it, aligned rows and both kernels for
-    rows that are not 16-byte multiples (class tiles / per-row re-aligning, forced through
-    ATTN_BWD_CLASS_ROWS / ATTN_BWD_RAGGED_ROWS), with and without clusters, against the
-    oracle (the variables are read once per process, hence the subprocess)."""
-    import os
-    import subprocess
-    import sys
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    through the library's test options where the shape allows it, aligned rows and both
+    kernels for rows that are not 16-byte multiples (class tiles / per-row re-aligning), with
+    and without clusters, against the oracle."""
     shapes = [(1, 100, 192), (1, 70, 640), (1, 40, 1280), (1, 33, 467), (1, 21, 901), (1, 17, 3001),
               (2, 7, 29), (1, 205, 333)]
-    code = _MODE_SCRIPT.format(root=root, pkg=os.path.join(root, "sol-1-advisor-token-fix_b200"), shapes=shapes)
-    env = dict(os.environ, ATTN_BWD_DS_MODE=mode)
-    env["ATTN_BWD_CLASS_ROWS" if rows == "class" else "ATTN_BWD_RAGGED_ROWS"] = "1"
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
-    assert r.returncode == 0, r.stderr[-2000:]
-    assert r.stdout.strip().startswith("OK"), r.stdout
+    bad = []
+    with ab.options(ds_mode=mode, row_kind=2 if rows == "class" else 1):
+        for shape in shapes:
+            data = generate_input(*shape, seed=31)
+            dS, dV = ab.custom_kernel(_to(data, cuda))
+            torch.cuda.synchronize()
+            rS, rV = attn_bwd_reference(data)
+            ok = (torch.allclose(rS.float(), dS.float().cpu(), rtol=RTOL, atol=ATOL) and
+                  torch.allclose(rV.float(), dV.float().cpu(), rtol=RTOL, atol=ATOL) and ab.poll_error() == 0)
+            if not ok:
+                bad.append(shape)
+    assert not bad, f"mode {mode} rows {rows}: mismatch on {bad}"
+
+
+def test_release_then_call_again(cuda):
+    """Releasing the library's per-device streams, events and cached graphs leaves it usable."""
+    data_cpu = generate_input(1, 96, 192, 46)
+    data = _to(data_cpu, cuda)
+    for _ in range(3):           # eager, captured, replayed
+        ab.custom_kernel(data)
+    ab.release()
+    dS, dV = ab.custom_kernel(data)
+    torch.cuda.synchronize()
+    rS, rV = attn_bwd_reference(data_cpu)
+    _close("dS after release", rS, dS)
+    _close("dV after release", rV, dV)
 
 
 def test_replayed_calls_follow_input_contents(cuda):
