@@ -81,6 +81,14 @@ enum Mode : int { kRecompute = 0, kResident = 1, kTmemP = 2, kCompact = 3 };
 enum RowKind : int { kRowsAligned = 0, kRowsRagged = 1, kRowsClass = 2 };
 constexpr int CLS_M_PITCH = 80;   // class rows: 64 B of mask row + 16 B (window may start 8 B into a word)
 
+// Stage counts of the aligned kCompact form (compile-time tuning overrides for measurements).
+#ifndef ATTN_BWD_CP_VST
+#define ATTN_BWD_CP_VST 2
+#endif
+#ifndef ATTN_BWD_CP_PST
+#define ATTN_BWD_CP_PST 6
+#endif
+
 // Shared-memory plan per mode.  With dP~ resident the MMAs of a unit end with
 // pass 1, so one dO buffer suffices and the freed space buys P/mask stages
 // (bytes in flight are what keep HBM busy).
@@ -97,8 +105,8 @@ struct Cfg {
   static constexpr bool TP = MODE == kTmemP;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
-  static constexpr int VST = RAG ? 2 : RES ? (TP ? 2 : 2) : 3;
-  static constexpr int PST = TP ? 4 : RAG ? (RES ? 4 : 3) : CLS ? (RES ? 5 : 3) : (RES ? 6 : 4);
+  static constexpr int VST = (CP && !CLS) ? ATTN_BWD_CP_VST : RAG ? 2 : RES ? 2 : 3;
+  static constexpr int PST = (CP && !CLS) ? ATTN_BWD_CP_PST : TP ? 4 : RAG ? (RES ? 4 : 3) : CLS ? (RES ? 5 : 3) : (RES ? 6 : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
   static constexpr int NSLOT = TP ? 5 : CP ? CP_SLOTS : TSLOTS;   // TMEM slots (<= 512 columns)
   static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
@@ -407,6 +415,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + C::OFF_MISC + 16);
   float* xb = reinterpret_cast<float*>(smem + C::OFF_XB);
 
+  ATTN_BWD_WAIT_STATS_BEGIN();
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
 
@@ -828,6 +837,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     const float scale = prm.scale;
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
     uint32_t job = 0, pi = 0, dsn = 0;
+    ATTN_BWD_SECT_INIT();
     bool cls_tma_unit = false, cls_row_ok = false;   // class rows: per unit / per thread's row
     int cls_s = 0;                                    // class rows: the unit's window shift
 
@@ -838,6 +848,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       const int slot = job % NSLOT;
       if (!warp_wait(&T_full[slot], (job / NSLOT) & 1, abort_flag, err, 0x0301)) return false;
       tc_fence_after();
+      ATTN_BWD_SECT(0);
       uint32_t v[16];
       tmem_ld16(tmem_base + t_lane + slot * SLOTC + cg * CW, v);
       tmem_wait_ld();
@@ -847,8 +858,10 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         if (lane == 0) mbar_arrive(&T_empty[slot]);
       }
       ++job;
+      ATTN_BWD_SECT(1);
       const int ps = pi % PST;
       if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0302)) return false;
+      ATTN_BWD_SECT(2);
       const unsigned long long el = row_el + (unsigned long long)c * BN;
       uint32_t pw[8], mw[4], mx[4];
       if constexpr (CLS)
@@ -858,6 +871,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         load_row<RAG>(smem_u32(smem + C::OFF_P + ps * C::P_BYTES), smem_u32(smem + C::OFF_M + ps * C::M_BYTES), row,
                       cg, uint32_t(el * 2) & 15u, uint32_t(el) & 15u, pw, mw);
       expand_mask(mw, use_mask, mx);
+      ATTN_BWD_SECT(3);
       // valid columns e in [lo, hi) of this thread's 16: ragged rows end inside the last
       // chunk; class windows also start s columns before the row in chunk 0
       int lo = 0, hi = CW;
@@ -867,31 +881,48 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         lo = min(max(-cb, 0), CW);
         hi = min(max(skv - cb, 0), CW);
       }
-      if ((RAG || CLS) && (lo > 0 || hi < CW)) {
-        // columns outside the row hold other rows' bytes
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (e < lo || e >= hi) mw[e >> 2] &= ~(0xFFu << ((e & 3) * 8));
-        if (!use_mask) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) mx[i] = 0;
+      const bool edge = (RAG || CLS) && (lo > 0 || hi < CW);
+      uint32_t m16[8];   // non-TP: 16-bit keep-masks of the 8 bf16 pairs
+      if constexpr (TP) {
+        if (edge) {
+          // columns outside the row hold other rows' bytes
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            if (e >= lo && e < hi) mx[e >> 2] |= 0xFFu << ((e & 3) * 8);
-        } else {
-          expand_mask(mw, use_mask, mx);
-        }
-      }
+            if (e < lo || e >= hi) mw[e >> 2] &= ~(0xFFu << ((e & 3) * 8));
+          if (!use_mask) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
-        acc0 = fmaf(__uint_as_float(v[2 * k]), __uint_as_float((pw[k] << 16) & m0), acc0);
-        acc1 = fmaf(__uint_as_float(v[2 * k + 1]), __uint_as_float(pw[k] & 0xFFFF0000u & m1), acc1);
-        if (TP) {
+            for (int i = 0; i < 4; ++i) mx[i] = 0;
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (e >= lo && e < hi) mx[e >> 2] |= 0xFFu << ((e & 3) * 8);
+          } else {
+            expand_mask(mw, use_mask, mx);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t m0 = mask_at(mx, 2 * k), m1 = mask_at(mx, 2 * k + 1);
+          acc0 = fmaf(__uint_as_float(v[2 * k]), __uint_as_float((pw[k] << 16) & m0), acc0);
+          acc1 = fmaf(__uint_as_float(v[2 * k + 1]), __uint_as_float(pw[k] & 0xFFFF0000u & m1), acc1);
           v[2 * k] &= m0;
           v[2 * k + 1] &= m1;
         }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m16[k] = use_mask ? mask16_pair(mw, k) : 0xFFFFFFFFu;
+        if (edge) {
+          // columns outside the row hold other rows' bytes
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (e < lo || e >= hi) m16[e >> 1] &= (e & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+        }
+        // acc += dP~ * (m * P), both lanes of a pair in one f32x2 FMA (same rounding as two fmaf)
+        uint64_t acc = f2(acc0, acc1);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = f2_fma(f2(v[2 * k], v[2 * k + 1]), bf16x2_to_f2(pw[k] & m16[k]), acc);
+        f2_split(acc, acc0, acc1);
       }
+      ATTN_BWD_SECT(4);
       // the stage goes back to the producer only after every lane has consumed what it
       // read from it (a release right after the loads let the next fill race them)
       __syncwarp();
@@ -907,10 +938,10 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         uint32_t tp[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          tp[k] = pack_bf16x2(__uint_as_float(v[2 * k] & mask_at(mx, 2 * k)),
-                              __uint_as_float(v[2 * k + 1] & mask_at(mx, 2 * k + 1)));
+          tp[k] = pack_bf16x2(__uint_as_float(v[2 * k]), __uint_as_float(v[2 * k + 1])) & m16[k];
         tmem_st8(tmem_base + t_lane + C::CP_BASE + cl * (BN / 2) + cg * (CW / 2), tp);
       }
+      ATTN_BWD_SECT(5);
       ++pi;
       return true;
     };
@@ -941,6 +972,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         for (int k = 0; k < cs; ++k) r += xr[k * BM];   // same order on every CTA
       }
       r *= scale;
+      ATTN_BWD_SECT(6);
       return true;
     };
 
@@ -1007,8 +1039,10 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           __syncwarp();
           if (lane == 0) mbar_arrive(&T_empty[slot]);
         }
+        ATTN_BWD_SECT(8);
         const int ps = pi % PST;
         if (!warp_wait(&PM_full[ps], (pi / PST) & 1, abort_flag, err, 0x0305)) return false;
+        ATTN_BWD_SECT(9);
         const unsigned long long el = row_el + (unsigned long long)c * BN;
         const uint32_t p_stage = smem_u32(smem + C::OFF_P + ps * C::P_BYTES);
         uint32_t pw[8], mw[4], mx[4];
@@ -1030,13 +1064,19 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
                           uint32_t(el) & 15u, pw, mw);
           expand_mask(mw, use_mask, mx);
         }
+        ATTN_BWD_SECT(10);
+        // dS = P * (m * dP~ * s - r), pairs in f32x2 (same rounding as the scalar fmaf / mul)
+        const uint64_t s2 = f2(scale, scale), nr2 = f2(-r, -r);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float t0 = __uint_as_float(v[2 * k] & mask_at(mx, 2 * k));
-          const float t1 = __uint_as_float(v[2 * k + 1] & mask_at(mx, 2 * k + 1));
-          const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
-          o[k] = pack_bf16x2(p0 * fmaf(t0, scale, -r), p1 * fmaf(t1, scale, -r));
+          uint32_t t0 = v[2 * k], t1 = v[2 * k + 1];
+          if (!CP) {   // kCompact's store already holds the masked dP~
+            t0 &= mask_at(mx, 2 * k);
+            t1 &= mask_at(mx, 2 * k + 1);
+          }
+          o[k] = pack_bf16x2_f2(f2_mul(bf16x2_to_f2(pw[k]), f2_fma(f2(t0, t1), s2, nr2)));
         }
+        ATTN_BWD_SECT(11);
         if (CLS && !cls_tma_unit_ok(cls_tma_unit, c, cls_s, skv)) {
           // class rows, a row's first / last chunk: this thread's 16 values are two
           // 16-byte aligned words of its row; words crossing the row end go element-wise
@@ -1068,6 +1108,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&dS_ready[ps]);
+          ATTN_BWD_SECT(12);
         } else {
           __syncwarp();
           if (lane == 0) mbar_arrive(&PM_empty[ps]);
@@ -1104,6 +1145,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       }
     }
   epi_done:
+    ATTN_BWD_SECT_FLUSH();
     __syncwarp();
   }
 
@@ -1115,6 +1157,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     tc_fence_after();
     tmem_dealloc(tmem_base, TSLOTS * BN);
   }
+  ATTN_BWD_WAIT_STATS_END();
 }
 
 }  // namespace ds

@@ -123,6 +123,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
+  ATTN_BWD_WAIT_STATS_BEGIN();
   const uint32_t warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 8); }
@@ -365,6 +366,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
     tc_fence_after();
     tmem_dealloc(tmem_base, 256);
   }
+  ATTN_BWD_WAIT_STATS_END();
 }
 
 }  // namespace dv

@@ -111,19 +111,56 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // ordering) and the outcome is agreed with a vote, so on a timeout the whole
 // warp leaves together and no lane is left behind in a __syncwarp.
 #ifdef ATTN_BWD_WAIT_STATS
-// Diagnostics builds only: cycles each warp spent in each wait site (index from the site code).
+// Diagnostics builds only: cycles each warp spent in each wait site (index from the site code),
+// summed per CTA in shared memory and added to the global counters once at the end of the
+// kernel (slot 127: the CTAs' total cycles), so the counting barely perturbs the timing.
 __device__ unsigned long long g_wait_cycles[128];
+__shared__ unsigned long long s_wait_cycles[128];
+__device__ __forceinline__ long long wait_stats_begin() {
+  if (threadIdx.x < 128) s_wait_cycles[threadIdx.x] = 0;
+  return clock64();
+}
+__device__ __forceinline__ void wait_stats_end(long long t0) {   // after the kernel's last __syncthreads
+  if (threadIdx.x == 0) s_wait_cycles[127] = (unsigned long long)(clock64() - t0);
+  __syncthreads();
+  if (threadIdx.x < 128 && s_wait_cycles[threadIdx.x]) atomicAdd(&g_wait_cycles[threadIdx.x], s_wait_cycles[threadIdx.x]);
+}
+// Section timer of the epilogue (diagnostics): cycles since the previous mark, per thread in
+// registers (32-bit), added to slot 64 + idx once at the end (ATTN_BWD_SECT_FLUSH).
+#define ATTN_BWD_SECT_INIT() \
+  uint32_t sect_t = (uint32_t)clock64(); \
+  uint32_t sect_acc[16] = {}
+#define ATTN_BWD_SECT(idx)                               \
+  do {                                                   \
+    const uint32_t sect_now = (uint32_t)clock64();       \
+    sect_acc[idx] += sect_now - sect_t;                  \
+    sect_t = sect_now;                                   \
+  } while (0)
+#define ATTN_BWD_SECT_FLUSH()                                                                        \
+  do {                                                                                               \
+    if ((threadIdx.x & 31) == 0)                                                                     \
+      for (int i_ = 0; i_ < 16; ++i_)                                                                \
+        if (sect_acc[i_]) atomicAdd(&sm100::s_wait_cycles[64 + i_], (unsigned long long)sect_acc[i_]); \
+  } while (0)
+#define ATTN_BWD_WAIT_STATS_BEGIN() const long long wait_stats_t0 = sm100::wait_stats_begin()
+#define ATTN_BWD_WAIT_STATS_END() sm100::wait_stats_end(wait_stats_t0)
+#else
+#define ATTN_BWD_SECT_INIT() (void)0
+#define ATTN_BWD_SECT(idx) (void)0
+#define ATTN_BWD_SECT_FLUSH() (void)0
+#define ATTN_BWD_WAIT_STATS_BEGIN() (void)0
+#define ATTN_BWD_WAIT_STATS_END() (void)0
 #endif
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
                                           int code) {
-#ifdef ATTN_BWD_WAIT_STATS
+#if defined(ATTN_BWD_WAIT_STATS) && !defined(ATTN_BWD_NO_WAIT_SITES)
   const long long t0 = clock64();
 #endif
   const bool ok = mbar_wait(bar, parity, abort, err, code);
   const bool all = __all_sync(0xffffffffu, ok);
-#ifdef ATTN_BWD_WAIT_STATS
+#if defined(ATTN_BWD_WAIT_STATS) && !defined(ATTN_BWD_NO_WAIT_SITES)
   if ((threadIdx.x & 31) == 0)
-    atomicAdd(&g_wait_cycles[(((code >> 8) & 0xF) * 8 + (code & 7)) & 127], (unsigned long long)(clock64() - t0));
+    atomicAdd(&s_wait_cycles[(((code >> 8) & 0xF) * 8 + (code & 7)) & 127], (unsigned long long)(clock64() - t0));
 #endif
   return all;
 }
@@ -429,6 +466,45 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one instruction computes both lanes, each
+// rounded exactly as the scalar fma.rn / mul.rn would.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t x, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(x));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// bf16 pair (lo in bits 0..15) widened to an fp32 pair
+__device__ __forceinline__ uint64_t bf16x2_to_f2(uint32_t w) { return f2(w << 16, w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack_bf16x2_f2(uint64_t x) {
+  float lo, hi;
+  f2_split(x, lo, hi);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Keep-mask of bf16 pair k (elements 2k, 2k+1) from 16 bool bytes in 4 words: 0xFFFF in
+// each 16-bit half whose byte is 1 (bytes are 0/1, so the multiply never carries).
+__device__ __forceinline__ uint32_t mask16_pair(const uint32_t (&mw)[4], int k) {
+  return __byte_perm(mw[k >> 1], 0u, (k & 1) ? 0x4342u : 0x4140u) * 0xFFFFu;
 }
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
