@@ -85,9 +85,6 @@ constexpr int CLS_M_PITCH = 80;   // class rows: 64 B of mask row + 16 B (window
 #ifndef ATTN_BWD_CP_VST
 #define ATTN_BWD_CP_VST 2
 #endif
-#ifndef ATTN_BWD_CLS_DOBUF
-#define ATTN_BWD_CLS_DOBUF 1
-#endif
 #ifndef ATTN_BWD_CP_PST
 #define ATTN_BWD_CP_PST 6
 #endif
@@ -106,17 +103,13 @@ struct Cfg {
   static constexpr int CP_BASE = CP_SLOTS * BN;        // kCompact: first column of the bf16 store
   static constexpr int CP_MAX = (TSLOTS * BN - CP_BASE) / (BN / 2);   // kCompact: chunks per CTA (10)
   static constexpr bool TP = MODE == kTmemP;
-  // dO tile buffers; class rows with dP~ resident may double-buffer the gathered tile
-  // (ATTN_BWD_CLS_DOBUF = 2, one P / mask stage fewer) so a unit's gather overlaps the
-  // previous unit
-  static constexpr bool CLS_RES = CLS && MODE == kResident;
-  static constexpr int DOBUF = CLS_RES ? ATTN_BWD_CLS_DOBUF : RES ? 1 : 2;
+  static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
   // CTA pairs: each CTA of the pair holds half of a V chunk (32 of its 64 rows), so the
   // same 32 KB hold four chunk stages instead of two
   static constexpr int V_STAGE = DUO ? V_BYTES / 2 : V_BYTES;
   static constexpr int VST = DUO ? 4 : (CP && !CLS) ? ATTN_BWD_CP_VST : RAG ? 2 : RES ? 2 : 3;
-  static constexpr int PST = (CP && !CLS) ? ATTN_BWD_CP_PST : TP ? 4 : RAG ? (RES ? 4 : 3) : CLS ? (CLS_RES ? (ATTN_BWD_CLS_DOBUF == 2 ? 4 : 5) : RES ? 5 : 3) : (RES ? 6 : 4);
+  static constexpr int PST = (CP && !CLS) ? ATTN_BWD_CP_PST : TP ? 4 : RAG ? (RES ? 4 : 3) : CLS ? (RES ? 5 : 3) : (RES ? 6 : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
   static constexpr int NSLOT = TP ? 5 : CP ? CP_SLOTS : TSLOTS;   // TMEM slots (<= 512 columns)
   static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
