@@ -157,8 +157,7 @@ enum {
   ATTN_BWD_OPT_SIDE_STREAM = 7,  /* 0: dS and dV back to back on the caller's stream */
   ATTN_BWD_OPT_GRAPH = 8,        /* 0: never replay full calls from cached CUDA graphs */
   ATTN_BWD_OPT_MAP_CACHE = 9,    /* 0: encode every TMA descriptor on every call */
-  ATTN_BWD_OPT_DUO = 10,         /* 1: CTA pairs (2-CTA M = 256 MMAs) in the dS kernel where the shape allows */
-  ATTN_BWD_OPT_COUNT = 11
+  ATTN_BWD_OPT_COUNT = 10
 };
 int attn_bwd_b200_set_option(int option, int value);
 /* Current value of an option (-1 = automatic), or -2 for an unknown option. */

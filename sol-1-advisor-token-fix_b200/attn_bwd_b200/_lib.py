@@ -34,7 +34,7 @@ SIGNATURES = {
 
 # Measurement / test options (ATTN_BWD_OPT_* in include/attn_bwd_b200.h); -1 = automatic.
 OPTIONS = {"ds_mode": 0, "row_kind": 1, "ds_cluster": 2, "l2_prefetch": 3, "l2_hint": 4, "split": 5,
-           "dv_sms": 6, "side_stream": 7, "graph": 8, "map_cache": 9, "duo": 10}
+           "dv_sms": 6, "side_stream": 7, "graph": 8, "map_cache": 9}
 
 _lib = None
 

@@ -78,13 +78,7 @@ bool set_ds_smem() {
          ATTN_BWD_SMEM(ds::kRowsRagged, ds::kRecompute) && ATTN_BWD_SMEM(ds::kRowsRagged, ds::kResident) &&
          ATTN_BWD_SMEM(ds::kRowsRagged, ds::kTmemP) && ATTN_BWD_SMEM(ds::kRowsClass, ds::kRecompute) &&
          ATTN_BWD_SMEM(ds::kRowsClass, ds::kResident) && ATTN_BWD_SMEM(ds::kRowsClass, ds::kTmemP) &&
-         ATTN_BWD_SMEM(ds::kRowsClass, ds::kCompact) &&
-         cudaFuncSetAttribute(ds::ds_kernel<ds::kRowsAligned, ds::kResident, true>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              ds::Cfg<ds::kRowsAligned, ds::kResident, true>::SMEM_BYTES) == cudaSuccess &&
-         cudaFuncSetAttribute(ds::ds_kernel<ds::kRowsAligned, ds::kCompact, true>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              ds::Cfg<ds::kRowsAligned, ds::kCompact, true>::SMEM_BYTES) == cudaSuccess;
+         ATTN_BWD_SMEM(ds::kRowsClass, ds::kCompact);
 #undef ATTN_BWD_SMEM
 }
 
@@ -344,19 +338,6 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
     prm.cpc = prm.nchunks;
   }
   prm.resident = mode != ds::kRecompute;
-  // CTA pairs (aligned rows held by one CTA, resident or compact form): two units of a kv group
-  // share one M = 256 MMA per chunk, each CTA loading half of the V chunk.  Option
-  // ATTN_BWD_OPT_DUO = 0 turns them off, 1 turns them on where the shape allows (default: off
-  // until measured).
-  const bool duo = rk == ds::kRowsAligned && prm.cs == 1 && (mode == ds::kResident || mode == ds::kCompact) &&
-                   prm.n_units % 2 == 0 && opt(ATTN_BWD_OPT_DUO) == 1;
-  if (duo) {
-    cuuint64_t dims[3] = {kHeadDim, (cuuint64_t)s.skv, (cuuint64_t)s.bs * kKvHeads};
-    cuuint64_t str[2] = {kHeadDim * 2, (cuuint64_t)s.skv * kHeadDim * 2};
-    cuuint32_t box[3] = {64, ds::BN / 2, 1};
-    if (!make_map(&tm_V, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, V, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
-      return ATTN_BWD_ETMAP;
-  }
   prm.bh_base = s.u0 * kGroups;
   prm.use_mask = p > 0.f ? 1 : 0;
   // L2 prefetch of a CTA's next unit during pass 2 (aligned rows only): measured on B200
@@ -393,12 +374,6 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   ATTN_BWD_PICK(ds::kRowsAligned, ds::kResident)
   ATTN_BWD_PICK(ds::kRowsAligned, ds::kTmemP)
   ATTN_BWD_PICK(ds::kRowsAligned, ds::kCompact)
-  if (duo) {
-    kern = mode == ds::kCompact ? ds::ds_kernel<ds::kRowsAligned, ds::kCompact, true>
-                                : ds::ds_kernel<ds::kRowsAligned, ds::kResident, true>;
-    smem = mode == ds::kCompact ? ds::Cfg<ds::kRowsAligned, ds::kCompact, true>::SMEM_BYTES
-                                : ds::Cfg<ds::kRowsAligned, ds::kResident, true>::SMEM_BYTES;
-  }
   ATTN_BWD_PICK(ds::kRowsRagged, ds::kRecompute)
   ATTN_BWD_PICK(ds::kRowsRagged, ds::kResident)
   ATTN_BWD_PICK(ds::kRowsRagged, ds::kTmemP)
@@ -414,34 +389,31 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   cfg.stream = stream;
   const int sm_budget = (max_ctas > 0 && max_ctas < st.sm_count) ? max_ctas : st.sm_count;
   int clusters = sm_budget;
-  const int cdim = duo ? 2 : prm.cs;   // CTAs per cluster: pairs, or a row's column split
-  if (cdim > 1) {
+  if (prm.cs > 1) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cdim;
+    attr[0].val.clusterDim.x = prm.cs;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cfg.gridDim = dim3(cdim * st.sm_count);
+    cfg.gridDim = dim3(prm.cs * st.sm_count);
     int max_clusters = 0;
     {
       std::lock_guard<std::mutex> lk(g_mu);
       DeviceState& mst = const_cast<DeviceState&>(st);
       for (int i = 0; i < mst.n_occ; ++i)
-        if (mst.occ[i].kern == (const void*)kern && mst.occ[i].cs == cdim) max_clusters = mst.occ[i].clusters;
+        if (mst.occ[i].kern == (const void*)kern && mst.occ[i].cs == prm.cs) max_clusters = mst.occ[i].clusters;
       if (!max_clusters) {
         if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters < 1)
           return ATTN_BWD_ECUDA;
-        if (mst.n_occ < 32) mst.occ[mst.n_occ++] = {(const void*)kern, cdim, max_clusters};
+        if (mst.n_occ < 32) mst.occ[mst.n_occ++] = {(const void*)kern, prm.cs, max_clusters};
       }
     }
     clusters = max_clusters;
-    if (clusters * cdim > sm_budget) clusters = sm_budget / cdim > 0 ? sm_budget / cdim : 1;
+    if (clusters * prm.cs > sm_budget) clusters = sm_budget / prm.cs > 0 ? sm_budget / prm.cs : 1;
   }
-  // work items per cluster: pairs of units (DUO), or units (each row's column split)
-  const int items = duo ? prm.n_units / 2 : prm.n_units;
-  const int n_clusters = items < clusters ? items : clusters;
-  cfg.gridDim = dim3(n_clusters * cdim);
+  const int n_clusters = prm.n_units < clusters ? prm.n_units : clusters;
+  cfg.gridDim = dim3(n_clusters * prm.cs);
   if (cudaLaunchKernelEx(&cfg, kern, tm_dO, tm_V, tm_P, tm_M, tm_dS, prm) != cudaSuccess) return ATTN_BWD_ECUDA;
   return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }

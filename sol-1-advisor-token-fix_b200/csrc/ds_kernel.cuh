@@ -92,7 +92,7 @@ constexpr int CLS_M_PITCH = 80;   // class rows: 64 B of mask row + 16 B (window
 // Shared-memory plan per mode.  With dP~ resident the MMAs of a unit end with
 // pass 1, so one dO buffer suffices and the freed space buys P/mask stages
 // (bytes in flight are what keep HBM busy).
-template <int RK, int MODE, bool DUO = false>
+template <int RK, int MODE>
 struct Cfg {
   static constexpr bool RAG = RK == kRowsRagged;
   static constexpr bool CLS = RK == kRowsClass;
@@ -105,10 +105,7 @@ struct Cfg {
   static constexpr bool TP = MODE == kTmemP;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
-  // CTA pairs: each CTA of the pair holds half of a V chunk (32 of its 64 rows), so the
-  // same 32 KB hold four chunk stages instead of two
-  static constexpr int V_STAGE = DUO ? V_BYTES / 2 : V_BYTES;
-  static constexpr int VST = DUO ? 4 : (CP && !CLS) ? ATTN_BWD_CP_VST : RAG ? 2 : RES ? 2 : 3;
+  static constexpr int VST = (CP && !CLS) ? ATTN_BWD_CP_VST : RAG ? 2 : RES ? 2 : 3;
   static constexpr int PST = (CP && !CLS) ? ATTN_BWD_CP_PST : TP ? 4 : RAG ? (RES ? 4 : 3) : CLS ? (RES ? 5 : 3) : (RES ? 6 : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
   static constexpr int NSLOT = TP ? 5 : CP ? CP_SLOTS : TSLOTS;   // TMEM slots (<= 512 columns)
@@ -121,7 +118,7 @@ struct Cfg {
   static constexpr int STG_BYTES = RAG ? kEpiWarps * 32 * STG_PITCH : 0;
   static constexpr int OFF_DO = 0;
   static constexpr int OFF_V = OFF_DO + DOBUF * DO_BYTES;
-  static constexpr int OFF_P = OFF_V + VST * V_STAGE;
+  static constexpr int OFF_P = OFF_V + VST * V_BYTES;
   static constexpr int OFF_M = OFF_P + PST * P_BYTES;
   static constexpr int OFF_STG = OFF_M + PST * M_BYTES;
   static constexpr int OFF_DST = OFF_STG + STG_BYTES;
@@ -380,13 +377,7 @@ __device__ __forceinline__ void cls_store_chunk(uint32_t tile, const ClsUnit& cu
   }
 }
 
-// DUO (aligned rows, one CTA per row, resident or compact form): CTA pairs.  The kernel
-// runs as 2-CTA clusters; the two CTAs of a pair take two units of the same (batch,
-// kv-head) and the leader (rank 0) issues one M = 256 MMA (tcgen05 cta_group::2) per chunk
-// for both: each CTA supplies its own 128 dO rows and half of the V chunk, and receives its
-// own rows' dP~ in its own TMEM.  Each CTA thus loads half the V bytes it would alone, and
-// the epilogue, P / mask traffic and dS stores stay per CTA.
-template <int RK, int MODE, bool DUO = false>
+template <int RK, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64,1,128,1) SW128
           const __grid_constant__ CUtensorMap tm_V,    // (d, skv, b·8)  box (64,64,1)    SW128
@@ -398,8 +389,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
                                                        // class: as tm_P
           const Params prm) {
   using namespace sm100;
-  using C = Cfg<RK, MODE, DUO>;
-  static_assert(!DUO || (RK == kRowsAligned && (MODE == kResident || MODE == kCompact)), "CTA pairs: aligned rows");
+  using C = Cfg<RK, MODE>;
   constexpr bool RAG = C::RAG, CLS = C::CLS;
   constexpr int PST = C::PST, VST = C::VST, DOBUF = C::DOBUF;
   constexpr bool RES = C::RES, TP = C::TP, HOLD = C::HOLD, CP = C::CP;
@@ -437,8 +427,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       mbar_init(&PM_empty[i], kEpiWarps);
       mbar_init(&dS_ready[i], kEpiWarps);
     }
-    // DUO: the leader's T_empty counts the epilogue warps of both CTAs
-    for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], (DUO ? 2 : 1) * kEpiWarps); }
+    for (int i = 0; i < TSLOTS; ++i) { mbar_init(&T_full[i], 1); mbar_init(&T_empty[i], kEpiWarps); }
     for (int i = 0; i < 4; ++i) mbar_init(&pair_bar[i], 32 * (kEpiWarps / 4));
     for (int i = 0; i < 2; ++i) mbar_init(&dS_free[i], 1);
     // every CTA of the cluster (itself included) arrives once per row per unit
@@ -453,17 +442,12 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     if (CLS && prm.cls_Y > 0) { prefetch_tmap(&tm_P); prefetch_tmap(&tm_M); prefetch_tmap(&tm_dS); }
   }
   if (warp == 1) {
-    if constexpr (DUO) {
-      tmem_alloc_pair(tmem_base_slot, TSLOTS * BN);
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(tmem_base_slot, TSLOTS * BN);
-      tmem_relinquish();
-    }
+    tmem_alloc(tmem_base_slot, TSLOTS * BN);
+    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
-  if (DUO || prm.cs > 1) cluster_sync();   // peers' barriers are initialised before any remote arrive
+  if (prm.cs > 1) cluster_sync();   // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
@@ -472,13 +456,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   // CTA `rank` owning chunks [c0, c0 + nloc) of every row; persistent over units
   // by cluster.  cs == 1: plain launch, one CTA owns whole rows.
   const int cs = prm.cs;
-  // DUO: crank is this CTA's rank in its pair; the pair takes units 2p, 2p+1 (same kv group,
-  // since every kv group has 10 x row-block units, an even count)
-  const int crank = (DUO || cs > 1) ? int(cluster_ctarank()) : 0;
-  const int rank = DUO ? 0 : crank;
+  const int rank = cs > 1 ? int(cluster_ctarank()) : 0;
   const int cid = int(blockIdx.x) / cs, ncl = int(gridDim.x) / cs;
-  const int u_first = DUO ? int(blockIdx.x & ~1u) + crank : cid;
-  const int u_step = DUO ? int(gridDim.x) : ncl;
   const int c0 = rank * prm.cpc;
   const int nloc = max(0, min(prm.cpc, nchunks - c0));
   const int sq = prm.sq, skv = prm.skv;
@@ -488,7 +467,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   if (warp == 0) {
     // ------------------------------------------------ dO / V producer (lane 0 issues)
     uint32_t vi = 0, di = 0;
-    for (int u = u_first; u < n_units; u += u_step) {
+    for (int u = cid; u < n_units; u += ncl) {
       int zv, vshift = 0;
       const int db = di % DOBUF;
       if (!warp_wait(&dO_empty[db], ((di / DOBUF) & 1) ^ 1, abort_flag, err, 0x0101)) goto producer_done;
@@ -529,17 +508,9 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         const int b = bh / kHeads, h = bh - b * kHeads;
         zv = b * kKvHeads + h / kGroups;
         if (lane == 0) {
-          if constexpr (DUO) {
-            // both CTAs' tiles complete on the leader's barrier, which expects them both
-            const uint32_t lb = mapa_shared(smem_u32(&dO_full[db]), 0);
-            if (crank == 0) mbar_arrive_expect_tx(&dO_full[db], 2 * DO_BYTES);
-            tma_load_4d_pair(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, lb, 0, h, mb * BM, b);
-            tma_load_4d_pair(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, lb, 64, h, mb * BM, b);
-          } else {
-            mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
-            tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
-            tma_load_4d(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
-          }
+          mbar_arrive_expect_tx(&dO_full[db], DO_BYTES);
+          tma_load_4d(smem + C::OFF_DO + db * DO_BYTES, &tm_dO, &dO_full[db], 0, h, mb * BM, b);
+          tma_load_4d(smem + C::OFF_DO + db * DO_BYTES + DO_BYTES / 2, &tm_dO, &dO_full[db], 64, h, mb * BM, b);
         }
       }
       ++di;
@@ -549,19 +520,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           const int vs = vi % VST;
           if (!warp_wait(&V_empty[vs], ((vi / VST) & 1) ^ 1, abort_flag, err, 0x0102)) goto producer_done;
           if (lane == 0) {
-            uint8_t* dst = smem + C::OFF_V + vs * C::V_STAGE;
-            if constexpr (DUO) {
-              // this CTA's half of the chunk: V rows c*64 + 32*crank .. +32 (the MMA's N split)
-              const uint32_t lb = mapa_shared(smem_u32(&V_full[vs]), 0);
-              if (crank == 0) mbar_arrive_expect_tx(&V_full[vs], V_BYTES);
-              tma_load_3d_pair(dst, &tm_V, lb, 0, c * BN + 32 * crank, zv);
-              tma_load_3d_pair(dst + C::V_STAGE / 2, &tm_V, lb, 64, c * BN + 32 * crank, zv);
-            } else {
-              mbar_arrive_expect_tx(&V_full[vs], V_BYTES);
-              // class rows: the window starts at column -s (V rows below 0 read as zeros)
-              tma_load_3d(dst, &tm_V, &V_full[vs], 0, c * BN - vshift, zv);
-              tma_load_3d(dst + V_BYTES / 2, &tm_V, &V_full[vs], 64, c * BN - vshift, zv);
-            }
+            mbar_arrive_expect_tx(&V_full[vs], V_BYTES);
+            uint8_t* dst = smem + C::OFF_V + vs * V_BYTES;
+            // class rows: the window starts at column -s (V rows below 0 read as zeros)
+            tma_load_3d(dst, &tm_V, &V_full[vs], 0, c * BN - vshift, zv);
+            tma_load_3d(dst + V_BYTES / 2, &tm_V, &V_full[vs], 64, c * BN - vshift, zv);
           }
           ++vi;
         }
@@ -569,10 +532,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     }
   producer_done:
     if (CLS) cp_async_wait_all();
-    // drain: the last issue of every stage must have landed before exit (DUO: the leader's
-    // barriers count both CTAs' copies, and the peer does not exit before the leader has
-    // drained them: both pass the final cluster barrier)
-    if (lane == 0 && (!DUO || crank == 0)) {
+    // drain: the last issue of every stage must have landed before exit
+    if (lane == 0) {
       for (uint32_t k = 0; k < uint32_t(DOBUF) && k < di; ++k) {
         const uint32_t i = di - 1 - k;
         mbar_drain(&dO_full[i % DOBUF], (i / DOBUF) & 1, err, 0x0111);
@@ -586,7 +547,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
   } else if (warp == 2 || (RAG && warp == 3)) {
     // ------------------------------------------------ P / mask producer (RAG: warps 2 and 3)
     uint32_t pi = 0;
-    for (int u = u_first; u < n_units; u += u_step) {
+    for (int u = cid; u < n_units; u += ncl) {
       const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
       ClsUnit cu;
       if constexpr (CLS) cu = cls_unit(u, prm);
@@ -664,8 +625,8 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
               // pass 2 re-reads this unit from L2, which leaves HBM idle for this CTA: pull
               // the same chunk of the CTA's next unit into L2 meanwhile, so that unit's
               // pass 1 finds it there
-              if (pass == 1 && prm.l2pf && u + u_step < n_units) {
-                const int un = u + u_step, bn_ = un / n_mb, mbn = un - bn_ * n_mb;
+              if (pass == 1 && prm.l2pf && u + ncl < n_units) {
+                const int un = u + ncl, bn_ = un / n_mb, mbn = un - bn_ * n_mb;
                 tma_prefetch_l2_3d(&tm_P, c * BN, mbn * BM, bn_);
                 tma_prefetch_l2_3d(&tm_M, c * BN, mbn * BM, bn_);
               }
@@ -708,10 +669,9 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (lane 0 issues)
-    constexpr uint32_t idesc = idesc_bf16_f32(DUO ? 2 * BM : BM, BN, false, false);
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
     uint32_t job = 0, vi = 0, di = 0;
-    if (DUO && crank != 0) goto mma_done;   // the leader issues the pair's MMAs
-    for (int u = u_first; u < n_units; u += u_step) {
+    for (int u = cid; u < n_units; u += ncl) {
       const int db = di % DOBUF;
       if (!warp_wait(&dO_full[db], (di / DOBUF) & 1, abort_flag, err, 0x0201)) goto mma_done;
       if (CLS) fence_proxy_async_smem();   // class rows: dO arrived by cp.async (generic proxy)
@@ -720,46 +680,30 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         for (int cl = 0; cl < nloc; ++cl) {
           (void)c0;  // chunk coordinates are not needed by the MMA (V chunk order matches)
           const int slot = job % NSLOT;
-          if (DUO ? !warp_wait_cluster(&T_empty[slot], ((job / NSLOT) & 1) ^ 1, abort_flag, err, 0x0202)
-                  : !warp_wait(&T_empty[slot], ((job / NSLOT) & 1) ^ 1, abort_flag, err, 0x0202))
-            goto mma_done;
+          if (!warp_wait(&T_empty[slot], ((job / NSLOT) & 1) ^ 1, abort_flag, err, 0x0202)) goto mma_done;
           const int vs = vi % VST;
           if (!warp_wait(&V_full[vs], (vi / VST) & 1, abort_flag, err, 0x0203)) goto mma_done;
           tc_fence_after();
           if (lane == 0) {
-            const uint32_t b_base = smem_u32(smem + C::OFF_V + vs * C::V_STAGE);
+            const uint32_t b_base = smem_u32(smem + C::OFF_V + vs * V_BYTES);
             const uint32_t d_tmem = tmem_base + slot * SLOTC;
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-              // 16 bf16 = 32 B step inside the 128 B swizzle atom; 64-column (d) halves of the dO
-              // tile 16 KB apart, of the V stage V_STAGE / 2 apart
+              // 16 bf16 = 32 B step inside the 128 B swizzle atom; 64-column halves 16 KB / 8 KB apart
               const uint32_t koff = (kk & 3) * 32;
               const uint64_t ad = sdesc_sw128(a_base + (kk >> 2) * (DO_BYTES / 2) + koff, 16, 1024);
-              const uint64_t bd = sdesc_sw128(b_base + (kk >> 2) * (C::V_STAGE / 2) + koff, 16, 1024);
-              if constexpr (DUO)
-                umma_bf16_pair(d_tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
-              else
-                umma_bf16(d_tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
+              const uint64_t bd = sdesc_sw128(b_base + (kk >> 2) * (V_BYTES / 2) + koff, 16, 1024);
+              umma_bf16(d_tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
             }
-            if constexpr (DUO) {
-              umma_commit_pair(&V_empty[vs]);
-              umma_commit_pair(&T_full[slot]);
-            } else {
-              umma_commit(&V_empty[vs]);
-              umma_commit(&T_full[slot]);
-            }
+            umma_commit(&V_empty[vs]);
+            umma_commit(&T_full[slot]);
           }
           __syncwarp();
           ++vi;
           ++job;
         }
       }
-      if (lane == 0) {
-        if constexpr (DUO)
-          umma_commit_pair(&dO_empty[db]);
-        else
-          umma_commit(&dO_empty[db]);
-      }
+      if (lane == 0) umma_commit(&dO_empty[db]);
       __syncwarp();
       ++di;
     }
@@ -773,7 +717,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       // kTmemP: dS of pass-2 chunk n is written into staging tile n % 2
       uint32_t n = 0;
       bool tp_pend = false;   // class rows: a TMA store of the previous tile may be reading it
-      for (int u = u_first; u < n_units; u += u_step) {
+      for (int u = cid; u < n_units; u += ncl) {
         const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
         ClsUnit cu;
         if constexpr (CLS) cu = cls_unit(u, prm);
@@ -826,7 +770,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     } else if constexpr (!RAG) {
       uint32_t pi = 0, dsr_par = 0;
       int npend = 0, pend0 = 0, pend1 = 0;   // stages whose store may still be reading (lane 0)
-      for (int u = u_first; u < n_units; u += u_step) {
+      for (int u = cid; u < n_units; u += ncl) {
         const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
         ClsUnit cu;
         if constexpr (CLS) cu = cls_unit(u, prm);
@@ -894,13 +838,6 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
     const uint32_t stg = smem_u32(smem + C::OFF_STG) + (warp - 4) * 32 * C::STG_PITCH;
     uint32_t job = 0, pi = 0, dsn = 0;
     ATTN_BWD_SECT_INIT();
-    // a TMEM slot goes back to the MMA issuer: DUO, to the leader's barrier (both CTAs arrive)
-    auto release_T = [&](int slot) {
-      if constexpr (DUO)
-        mbar_arrive_remote(mapa_shared(smem_u32(&T_empty[slot]), 0));
-      else
-        mbar_arrive(&T_empty[slot]);
-    };
     bool cls_tma_unit = false, cls_row_ok = false;   // class rows: per unit / per thread's row
     int cls_s = 0;                                    // class rows: the unit's window shift
 
@@ -918,7 +855,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
       if (!HOLD) {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) release_T(slot);
+        if (lane == 0) mbar_arrive(&T_empty[slot]);
       }
       ++job;
       ATTN_BWD_SECT(1);
@@ -1051,7 +988,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) release_T(slot);
+        if (lane == 0) mbar_arrive(&T_empty[slot]);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float p0 = __uint_as_float(pw[k] << 16), p1 = __uint_as_float(pw[k] & 0xFFFF0000u);
@@ -1100,7 +1037,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) release_T(slot);
+          if (lane == 0) mbar_arrive(&T_empty[slot]);
         }
         ATTN_BWD_SECT(8);
         const int ps = pi % PST;
@@ -1184,7 +1121,7 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
 
     {
       uint32_t it = 0;
-      for (int u = u_first; u < n_units; u += u_step, ++it) {
+      for (int u = cid; u < n_units; u += ncl, ++it) {
         const int bhl = CLS ? 0 : u / n_mb, mb = CLS ? 0 : u - bhl * n_mb;
         unsigned long long row_el = CLS ? 0ull : ((unsigned long long)bhl * sq + mb * BM + row) * skv;
         int mo = 0;
@@ -1214,14 +1151,11 @@ ds_kernel(const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)   box (64
 
   tc_fence_before();
   __syncthreads();
-  if (DUO || prm.cs > 1) cluster_sync();   // no CTA leaves while a peer may still write into its shared memory
+  if (prm.cs > 1) cluster_sync();   // no CTA leaves while a peer may still write into its shared memory
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    if constexpr (DUO)
-      tmem_dealloc_pair(tmem_base, TSLOTS * BN);
-    else
-      tmem_dealloc(tmem_base, TSLOTS * BN);
+    tmem_dealloc(tmem_base, TSLOTS * BN);
   }
   ATTN_BWD_WAIT_STATS_END();
 }
