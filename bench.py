@@ -38,7 +38,10 @@ CONFIGS = {"c0": (2, 64, 96), "c1": (6, 384, 384), "c2": (12, 301, 467),
            "c3": (2, 2048, 3072), "c4": (48, 640, 640),
            # profiling stand-in: 4 of c4's 48 batch rows (same kernel mode, ~1 GB), so that
            # an ncu capture stays small; its DRAM traffic scales to c4 by 48/4
-           "c4s": (4, 640, 640)}
+           "c4s": (4, 640, 640),
+           # profiling stand-in for c3: same row length, hence the same cluster form (6 CTAs per
+           # row, dP~ resident), a quarter of its rows (~0.9 GB)
+           "c3s": (1, 1024, 3072)}
 H, KVH, G, D = 80, 8, 10, 128
 FALLBACK_HBM_GBS = 6650.0
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one dS-kernel launch per
