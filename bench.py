@@ -46,9 +46,9 @@ H, KVH, G, D = 80, 8, 10, 128
 FALLBACK_HBM_GBS = 6650.0
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one dS-kernel launch per
 # (batch, kv-head) unit, from the ncu --set full capture of `bench.py --config c4s --once`
-# (c4s = 4 of c4's 48 batch rows, same kernel mode; 669.11 MB over 32 units), scaled by the
+# (c4s = 4 of c4's 48 batch rows, same kernel mode; 669.30 MB over 32 units), scaled by the
 # units a launch processes.  Only used for the c4 workload's roofline line.
-DS_TRAFFIC_PER_UNIT = {"c4": 669.107e6 / 32}
+DS_TRAFFIC_PER_UNIT = {"c4": 669.298e6 / 32}
 
 
 def alg_bytes(units, sq, skv):
