@@ -82,6 +82,19 @@ enum RowKind : int { kRowsAligned = 0, kRowsRagged = 1, kRowsClass = 2 };
 constexpr int CLS_M_PITCH = 80;   // class rows: 64 B of mask row + 16 B (window may start 8 B into a word)
 
 // Stage counts of the aligned kCompact form (compile-time tuning overrides for measurements).
+#ifndef ATTN_BWD_RES_VST
+#define ATTN_BWD_RES_VST 2
+#endif
+#ifndef ATTN_BWD_RES_PST
+#define ATTN_BWD_RES_PST 6
+#endif
+// class-tile rows with dP~ resident: a third V stage fits beside the five P / mask stages and
+// lets the MMA run further ahead of the epilogue (c2 dS 237.5 -> 227.4 us, 8x373x449 204.8 ->
+// 198.8 us).  Aligned resident rows keep 2 V + 6 P / mask stages (3 + 5 measured +2 % on c1,
+// -3 % on c3's clusters).
+#ifndef ATTN_BWD_CLS_VST
+#define ATTN_BWD_CLS_VST 3
+#endif
 #ifndef ATTN_BWD_CP_VST
 #define ATTN_BWD_CP_VST 2
 #endif
@@ -105,8 +118,12 @@ struct Cfg {
   static constexpr bool TP = MODE == kTmemP;
   static constexpr int DOBUF = RES ? 1 : 2;            // dO tile buffers
   // V chunk stages (aligned non-resident: V read twice); P/mask chunk stages
-  static constexpr int VST = (CP && !CLS) ? ATTN_BWD_CP_VST : RAG ? 2 : RES ? 2 : 3;
-  static constexpr int PST = (CP && !CLS) ? ATTN_BWD_CP_PST : TP ? 4 : RAG ? (RES ? 4 : 3) : CLS ? (RES ? 5 : 3) : (RES ? 6 : 4);
+  static constexpr bool ALRES = RK == kRowsAligned && MODE == kResident;
+  static constexpr bool CLSRES = CLS && MODE == kResident;
+  static constexpr int VST = (CP && !CLS) ? ATTN_BWD_CP_VST : ALRES ? ATTN_BWD_RES_VST : CLSRES ? ATTN_BWD_CLS_VST
+                           : RAG ? 2 : RES ? 2 : 3;
+  static constexpr int PST = (CP && !CLS) ? ATTN_BWD_CP_PST : ALRES ? ATTN_BWD_RES_PST : TP ? 4 : RAG ? (RES ? 4 : 3)
+                           : CLS ? (RES ? 5 : 3) : (RES ? 6 : 4);
   static constexpr int SLOTC = TP ? 96 : BN;           // TMEM columns per chunk slot
   static constexpr int NSLOT = TP ? 5 : CP ? CP_SLOTS : TSLOTS;   // TMEM slots (<= 512 columns)
   static constexpr int DST_BYTES = (TP && !RAG) ? 2 * BM * BN * 2 : 0;   // dS staging tiles (SW128)
