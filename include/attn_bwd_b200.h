@@ -81,6 +81,21 @@ int attn_bwd_b200_dv_shard(const void* grad_attn_output, const void* attn_weight
                            int seq_kv, int unit_begin, int unit_end, void* grad_value_states,
                            attn_bwd_stream_t stream);
 
+/* Full call without attn_weights_dropped.  The dV kernel forms each K chunk of P_drop in
+ * shared memory as bf16(P * mask * 1/(1-p)) from the attn_weights and dropout_mask tiles it
+ * streams, which is how the reference's inputs are made (eval_modal_attn_bwd.py:159-161:
+ * attn_weights_dropped = bf16(attn_weights * mask / (1-p))).  Valid only for callers whose
+ * P_drop is that product: it does NOT reproduce the reference for an arbitrary P_drop
+ * (starting_point.py:62-64 reads the given tensor).  A caller using it never materialises
+ * P_drop (2 bytes per score element of memory, and its host->device copy).  Requires
+ * 0 <= attention_dropout < 1 (else ATTN_BWD_EINVAL) and seq_kv % 16 == 0 (else
+ * ATTN_BWD_EUNSUPPORTED).  Sharding arguments as attn_bwd_b200_shard.  Replaces nothing in
+ * the reference: it is the optional P_drop-free variant, behind its own entry point. */
+int attn_bwd_b200_shard_from_mask(const void* grad_attn_output, const void* attn_weights, const void* value_states,
+                                  const uint8_t* dropout_mask, float attention_dropout, int bs, int seq_q, int seq_kv,
+                                  int unit_begin, int unit_end, void* grad_attn_scores, void* grad_value_states,
+                                  attn_bwd_stream_t stream);
+
 /* Host-buffer call: the same result as attn_bwd_b200_shard for inputs and outputs that live
  * in HOST memory, for callers whose tensors are not yet on the GPU.  The reference's
  * custom_kernel (starting_point.py:27-70) takes device tensors and has no such form; this

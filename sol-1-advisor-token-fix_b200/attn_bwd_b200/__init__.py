@@ -19,7 +19,7 @@ NUM_GROUPS = NUM_ATTENTION_HEADS // NUM_KEY_VALUE_HEADS
 HEAD_DIM = 128
 
 __all__ = ["custom_kernel", "attn_bwd", "attn_bwd_shard", "attn_bwd_host", "ds_shard", "dv_shard", "run",
-           "AttnBwdError", "poll_error", "release", "options", "NUM_ATTENTION_HEADS", "NUM_KEY_VALUE_HEADS",
+           "AttnBwdError", "poll_error", "release", "options", "attn_bwd_from_mask", "NUM_ATTENTION_HEADS", "NUM_KEY_VALUE_HEADS",
            "HEAD_DIM"]
 
 
@@ -297,6 +297,35 @@ def run(grad_attn_output, attn_weights, attn_weights_dropped, value_states, drop
     (append.py:29-33)."""
     return custom_kernel((grad_attn_output, attn_weights, attn_weights_dropped, value_states,
                           dropout_mask, attention_dropout))
+
+
+def attn_bwd_from_mask(data, unit_begin=None, unit_end=None, out=None):
+    """The full call WITHOUT attn_weights_dropped (C-ABI ``attn_bwd_b200_shard_from_mask``):
+    the dV kernel forms P_drop = bf16(attn_weights * dropout_mask / (1 - p)) itself.
+
+    Only valid when the caller's P_drop is that product, which is how the reference's
+    inputs are made (eval_modal_attn_bwd.py:159-161); for any other P_drop use
+    :func:`custom_kernel`.  ``data`` is the reference tuple with attn_weights_dropped
+    ignored (it may be None).  Needs 0 <= p < 1 and seq_kv % 16 == 0.  With a unit range the
+    shard conventions of :func:`attn_bwd_shard` apply and (dS_shard, dV_shard) come back;
+    without, the reference's output shapes."""
+    dO, P, _, V, M, p = data
+    full = unit_begin is None and unit_end is None
+    dO, P, _, V, M, p, bs, sq, skv, u0, u1 = _check_inputs((dO, P, None, V, M, p), unit_begin, unit_end)
+    nh = (u1 - u0) * NUM_GROUPS
+    with torch.cuda.device(dO.device):
+        if out is None:
+            if full:
+                dS = torch.empty((bs, NUM_ATTENTION_HEADS, sq, skv), dtype=torch.bfloat16, device=dO.device)
+                dV = torch.empty((bs, NUM_KEY_VALUE_HEADS, skv, HEAD_DIM), dtype=torch.bfloat16, device=dO.device)
+            else:
+                dS = torch.empty((nh, sq, skv), dtype=torch.bfloat16, device=dO.device)
+                dV = torch.empty((u1 - u0, skv, HEAD_DIM), dtype=torch.bfloat16, device=dO.device)
+        else:
+            dS, dV = out
+        _lib.call("attn_bwd_b200_shard_from_mask", _ptr(dO), _ptr(P), _ptr(V), _ptr(M), p, bs, sq, skv, u0, u1,
+                  _ptr(dS), _ptr(dV), _stream())
+    return dS, dV
 
 
 def ds_shard(dO, P, V, M, p, unit_begin, unit_end, out=None):

@@ -21,6 +21,7 @@ SIGNATURES = {
     "attn_bwd_b200_shard": (_I, [_VP, _VP, _VP, _VP, _VP, _F, _I, _I, _I, _I, _I, _VP, _VP, _VP]),
     "attn_bwd_b200_ds_shard": (_I, [_VP, _VP, _VP, _VP, _F, _I, _I, _I, _I, _I, _VP, _VP]),
     "attn_bwd_b200_dv_shard": (_I, [_VP, _VP, _I, _I, _I, _I, _I, _VP, _VP]),
+    "attn_bwd_b200_shard_from_mask": (_I, [_VP, _VP, _VP, _VP, _F, _I, _I, _I, _I, _I, _VP, _VP, _VP]),
     "attn_bwd_b200_host_shard": (_I, [_VP] * 5 + [_F, _I, _I, _I, _I, _I] + [_VP] * 9 + [_I, _VP]),
     "attn_bwd_b200_host": (_I, [_VP] * 5 + [_F, _I, _I, _I] + [_VP] * 9 + [_I, _VP]),
     "attn_bwd_b200_poll_error": (_I, []),

@@ -100,6 +100,8 @@ int device_state(DeviceState** out) {
                                     dv::Cfg<false>::SMEM_BYTES) != cudaSuccess ||
                cudaFuncSetAttribute(dv::dv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     dv::Cfg<true>::SMEM_BYTES) != cudaSuccess ||
+               cudaFuncSetAttribute(dv::dv_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    dv::Cfg<false, true>::SMEM_BYTES) != cudaSuccess ||
                cudaGetSymbolAddress(reinterpret_cast<void**>(&st.err), g_kernel_error) != cudaSuccess) {
       st.rc = ATTN_BWD_ECUDA;
     }
@@ -418,8 +420,11 @@ int launch_ds(const DeviceState& st, const Shape& s, const void* dO, const void*
   return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 
+// Pd is attn_weights_dropped; or, with M != nullptr, attn_weights, and the kernel forms
+// P_drop = bf16(P * M / (1-p)) itself (seq_kv % 16 == 0 only).
 int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void* Pd, void* dV,
-              cudaStream_t stream, int max_ctas = 0) {
+              cudaStream_t stream, int max_ctas = 0, const uint8_t* M = nullptr, float p = 0.f) {
+  const bool fpm = M != nullptr;
   const int nu = s.n_units();
   if (nu == 0 || s.skv == 0) return ATTN_BWD_OK;
   if (s.sq == 0) {  // empty sum over seq_q: dV = 0
@@ -428,8 +433,18 @@ int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void*
   }
   // P_drop rows need only be 16-byte multiples (seq_kv % 8) for the TMA path
   const bool rag = (s.skv % 8) != 0;
-  CUtensorMap tm_Pd, tm_dO;
+  if (fpm && rag) return ATTN_BWD_EUNSUPPORTED;
+  CUtensorMap tm_Pd, tm_dO, tm_M;
   std::memset(&tm_Pd, 0, sizeof(tm_Pd));
+  std::memset(&tm_M, 0, sizeof(tm_M));
+  if (fpm) {
+    if (s.skv % 16) return ATTN_BWD_EUNSUPPORTED;   // mask rows must be 16-byte multiples for TMA
+    cuuint64_t dims[3] = {(cuuint64_t)s.skv, (cuuint64_t)s.sq, (cuuint64_t)nu * kGroups};
+    cuuint64_t str[2] = {(cuuint64_t)s.skv, (cuuint64_t)s.sq * s.skv};
+    cuuint32_t box[3] = {dv::BM, dv::BK, 1};
+    if (!make_map(&tm_M, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, M, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return ATTN_BWD_ETMAP;
+  }
   if (!rag) {
     cuuint64_t dims[3] = {(cuuint64_t)s.skv, (cuuint64_t)s.sq, (cuuint64_t)nu * kGroups};
     cuuint64_t str[2] = {(cuuint64_t)s.skv * 2, (cuuint64_t)s.sq * s.skv * 2};
@@ -465,13 +480,19 @@ int launch_dv(const DeviceState& st, const Shape& s, const void* dO, const void*
   prm.Pd = static_cast<const uint8_t*>(Pd);
   prm.pd_end16 = ((unsigned long long)nu * kGroups * s.sq * s.skv * 2 + 15) & ~15ull;
   prm.tma_rows = rows8 * 8;
+  prm.scale = fpm ? 1.0f / (1.0f - p) : 1.0f;
   int grid = prm.n_units < st.sm_count ? prm.n_units : st.sm_count;
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(dV);
   if (rag)
-    dv::dv_kernel<true><<<grid, dv::Cfg<true>::kThreads, dv::Cfg<true>::SMEM_BYTES, stream>>>(tm_Pd, tm_dO, out, prm);
+    dv::dv_kernel<true><<<grid, dv::Cfg<true>::kThreads, dv::Cfg<true>::SMEM_BYTES, stream>>>(tm_Pd, tm_dO, out, prm,
+                                                                                            tm_M);
+  else if (fpm)
+    dv::dv_kernel<false, true><<<grid, dv::Cfg<false, true>::kThreads, dv::Cfg<false, true>::SMEM_BYTES, stream>>>(
+        tm_Pd, tm_dO, out, prm, tm_M);
   else
-    dv::dv_kernel<false><<<grid, dv::Cfg<false>::kThreads, dv::Cfg<false>::SMEM_BYTES, stream>>>(tm_Pd, tm_dO, out, prm);
+    dv::dv_kernel<false><<<grid, dv::Cfg<false>::kThreads, dv::Cfg<false>::SMEM_BYTES, stream>>>(tm_Pd, tm_dO, out, prm,
+                                                                                             tm_M);
   return cudaPeekAtLastError() == cudaSuccess ? ATTN_BWD_OK : ATTN_BWD_ECUDA;
 }
 
@@ -499,8 +520,11 @@ int prologue(DeviceState** st, const Shape& s) {
 
 
 // Issues the dS and dV kernels of one full call on stream cs (see attn_bwd_b200_shard).
+// fpm: the dV kernel forms P_drop from P and the mask (Pd unused).
 int enqueue_full_locked(DeviceState* st, const Shape& s, const void* dO, const void* P, const void* Pd, const void* V,
-                 const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs) {
+                 const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs, bool fpm = false) {
+  const void* dv_src = fpm ? P : Pd;
+  const uint8_t* dv_mask = fpm ? M : nullptr;
   int rc = ATTN_BWD_OK;
   // The dS and dV kernels are independent (different inputs and outputs), so the dV
   // kernel always runs on a side stream forked from the caller's stream, which waits for
@@ -540,11 +564,11 @@ int enqueue_full_locked(DeviceState* st, const Shape& s, const void* dO, const v
     if (cudaEventRecord(st->fork, cs) != cudaSuccess || cudaStreamWaitEvent(st->side, st->fork, 0) != cudaSuccess)
       return ATTN_BWD_ECUDA;
     if (split) {
-      rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side, dv_grid);
+      rc_dv = launch_dv(*st, s, dO, dv_src, dV, st->side, dv_grid, dv_mask, p);
       if (rc_dv == ATTN_BWD_OK) rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs, budget);
     } else {
       rc_ds = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
-      if (rc_ds == ATTN_BWD_OK) rc_dv = launch_dv(*st, s, dO, Pd, dV, st->side);
+      if (rc_ds == ATTN_BWD_OK) rc_dv = launch_dv(*st, s, dO, dv_src, dV, st->side, 0, dv_mask, p);
     }
     // join even after an error, so the caller's stream never runs ahead of issued work
     if (cudaEventRecord(st->join, st->side) != cudaSuccess || cudaStreamWaitEvent(cs, st->join, 0) != cudaSuccess)
@@ -553,14 +577,14 @@ int enqueue_full_locked(DeviceState* st, const Shape& s, const void* dO, const v
   }
   rc = launch_ds(*st, s, dO, P, V, M, p, dS, cs);
   if (rc) return rc;
-  return launch_dv(*st, s, dO, Pd, dV, cs);
+  return launch_dv(*st, s, dO, dv_src, dV, cs, 0, dv_mask, p);
 }
 
 
 int enqueue_full(DeviceState* st, const Shape& s, const void* dO, const void* P, const void* Pd, const void* V,
-                 const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs) {
+                 const uint8_t* M, float p, void* dS, void* dV, cudaStream_t cs, bool fpm = false) {
   std::lock_guard<std::mutex> lk(st->side_mu);
-  return enqueue_full_locked(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
+  return enqueue_full_locked(st, s, dO, P, Pd, V, M, p, dS, dV, cs, fpm);
 }
 
 // A full call as a CUDA graph: the first sighting of an argument list runs eagerly, the
@@ -780,6 +804,22 @@ int attn_bwd_b200_shard(const void* dO, const void* P, const void* Pd, const voi
     return ATTN_BWD_EALIGN;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   return run_full(st, s, dO, P, Pd, V, M, p, dS, dV, cs);
+}
+
+int attn_bwd_b200_shard_from_mask(const void* dO, const void* P, const void* V, const uint8_t* M, float p, int bs,
+                                  int sq, int skv, int u0, int u1, void* dS, void* dV, attn_bwd_stream_t stream) {
+  if (!(p >= 0.f && p < 1.f)) return ATTN_BWD_EINVAL;
+  Shape s{bs, sq, skv, u0, u1};
+  DeviceState* st = nullptr;
+  int rc = prologue(&st, s);
+  if (rc) return rc;
+  if (!ptr_ok(dO, s.n_dO()) || !ptr_ok(P, s.n_scores()) || !ptr_ok(V, s.n_V()) || !ptr_ok(M, s.n_scores()) ||
+      !ptr_ok(dS, s.n_scores()) || !ptr_ok(dV, s.n_dV()))
+    return ATTN_BWD_EINVAL;
+  if (!aligned16(dO) || !aligned16(P) || !aligned16(V) || !aligned16(M) || !aligned16(dS) || !aligned16(dV))
+    return ATTN_BWD_EALIGN;
+  if (s.n_units() > 0 && s.sq > 0 && s.skv % 16) return ATTN_BWD_EUNSUPPORTED;
+  return enqueue_full(st, s, dO, P, nullptr, V, M, p, dS, dV, reinterpret_cast<cudaStream_t>(stream), true);
 }
 
 int attn_bwd_b200(const void* dO, const void* P, const void* Pd, const void* V, const uint8_t* M, float p, int bs,

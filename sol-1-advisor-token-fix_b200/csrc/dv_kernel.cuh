@@ -38,15 +38,22 @@ constexpr int A_BYTES = BK * BM * 2;          // 16 KB (two 64-col MN blocks of 
 constexpr int B_BYTES = BK * kHeadDim * 2;    // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 
-template <bool RAG>
+// FPM (aligned rows only): P_drop is not read; each K chunk's A tile is formed in shared
+// memory from attn_weights and the dropout mask as bf16(P · m · 1/(1-p)), the identity by
+// which the reference's inputs are made (eval_modal_attn_bwd.py:159-161).  Warps 6..13 convert
+// a stage in place once its P and mask tiles have landed.
+template <bool RAG, bool FPM = false>
 struct Cfg {
-  static constexpr int kThreads = RAG ? 480 : 192;    // RAG: + 8 re-align warps (6..13), raw producer (14)
-  static constexpr int ST = RAG ? 4 : 6;               // operand stages (RAG: 3 + 6 raw measured slower)
+  static constexpr int kThreads = RAG ? 480 : FPM ? 448 : 192;   // RAG: + 8 re-align warps (6..13), raw producer (14)
+  static constexpr int ST = RAG ? 4 : FPM ? 5 : 6;     // operand stages (RAG: 3 + 6 raw measured slower)
+  static constexpr int MSK_BYTES = FPM ? BK * BM : 0;  // FPM: mask tile per stage (64 rows x 128 B, SW128)
+  static constexpr int A_READY = 8;                    // warps that arrive on a_ready (re-align / convert)
   static constexpr int RST = RAG ? 4 : 0;              // raw P_drop row stages
   static constexpr int RAW_PITCH = 272;                // 256 B of row + 16 B of misalignment slack
   static constexpr int CLS_BYTES = 8 * RAW_PITCH;      // one class box: 8 rows (2176 B, 128-byte multiple)
   static constexpr int RAW_BYTES = BK * RAW_PITCH;
-  static constexpr int OFF_RAW = ST * STAGE_BYTES;
+  static constexpr int OFF_MSK = ST * STAGE_BYTES;
+  static constexpr int OFF_RAW = OFF_MSK + ST * MSK_BYTES;
   static constexpr int OFF_BAR = OFF_RAW + RST * RAW_BYTES;
   static constexpr int NBAR = 3 * ST + 2 * RST + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
@@ -64,6 +71,7 @@ struct Params {
   const uint8_t* Pd;              // local P_drop base (RAG path)
   unsigned long long pd_end16;    // bytes of P_drop rounded up to 16
   long long tma_rows;             // RAG: rows covered by the class tensor map (8 · floor(rows / 8))
+  float scale;                    // FPM: 1 / (1 - p)
 };
 
 // out[j] = bytes [4j+sh, 4j+sh+4) of the little-endian stream `in` (NOUT+4 words).
@@ -99,15 +107,18 @@ __device__ __forceinline__ void raw_rows_sync(uint32_t rdst, const Params& prm, 
   sm100::cp_async_wait_all();
 }
 
-template <bool RAG>
-__global__ void __launch_bounds__(Cfg<RAG>::kThreads, 1)
+template <bool RAG, bool FPM = false>
+__global__ void __launch_bounds__(Cfg<RAG, FPM>::kThreads, 1)
 dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_local) box (64,64,1) SW128;
-                                                       // RAG: u32 (4·skv, rows/8) box (68, 8), no swizzle
+                                                       // RAG: u32 (4·skv, rows/8) box (68, 8), no swizzle;
+                                                       // FPM: attn_weights, as aligned
           const __grid_constant__ CUtensorMap tm_dO,   // (d, h, s, b)         box (64,1,64,1) SW128
           __nv_bfloat16* __restrict__ dV,              // local [units, skv, 128]
-          const Params prm) {
+          const Params prm,
+          const __grid_constant__ CUtensorMap tm_M) {  // FPM: mask u8 (skv, sq, bh_local) box (128,64,1) SW128
   using namespace sm100;
-  using C = Cfg<RAG>;
+  using C = Cfg<RAG, FPM>;
+  static_assert(!(RAG && FPM), "P_drop from P and mask: aligned rows only");
   constexpr int ST = C::ST, RST = C::RST;
   constexpr int RSTD = RST > 0 ? RST : 1;  // keeps the (unused) ragged arithmetic defined when RST == 0
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -126,7 +137,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
   ATTN_BWD_WAIT_STATS_BEGIN();
   const uint32_t warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], 8); }
+    for (int i = 0; i < ST; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); mbar_init(&a_ready[i], C::A_READY); }
     // raw_full: the producer's lane 0 (with the class boxes' bytes as transaction count)
     for (int i = 0; i < RST; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
@@ -136,6 +147,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
   if (warp == 0 && lane == 0) {
     if (!RAG || prm.tma_rows > 0) prefetch_tmap(&tm_Pd);
     prefetch_tmap(&tm_dO);
+    if (FPM) prefetch_tmap(&tm_M);
   }
   if (warp == 1) { tmem_alloc(tmem_base_slot, 256); tmem_relinquish(); }
   tc_fence_before();
@@ -161,11 +173,12 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
             {
               uint8_t* a = smem + s * STAGE_BYTES;
               uint8_t* bsm = a + A_BYTES;
-              mbar_arrive_expect_tx(&full[s], RAG ? B_BYTES : STAGE_BYTES);
+              mbar_arrive_expect_tx(&full[s], RAG ? B_BYTES : STAGE_BYTES + C::MSK_BYTES);
               if (!RAG) {
                 tma_load_3d(a, &tm_Pd, &full[s], jt * BM, kc * BK, bhl);
                 tma_load_3d(a + A_BYTES / 2, &tm_Pd, &full[s], jt * BM + 64, kc * BK, bhl);
               }
+              if (FPM) tma_load_3d(smem + C::OFF_MSK + s * C::MSK_BYTES, &tm_M, &full[s], jt * BM, kc * BK, bhl);
               tma_load_4d(bsm, &tm_dO, &full[s], 0, h, kc * BK, b);
               tma_load_4d(bsm + B_BYTES / 2, &tm_dO, &full[s], 64, h, kc * BK, b);
             }
@@ -196,7 +209,7 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
         for (int k = 0; k < nk; ++k) {
           const int s = si % ST;
           if (!warp_wait(&full[s], (si / ST) & 1, abort_flag, err, 0x1202)) goto mma_done;
-          if (RAG && !warp_wait(&a_ready[s], (si / ST) & 1, abort_flag, err, 0x1203)) goto mma_done;
+          if ((RAG || FPM) && !warp_wait(&a_ready[s], (si / ST) & 1, abort_flag, err, 0x1203)) goto mma_done;
           tc_fence_after();
           if (lane == 0) {
             const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
@@ -256,6 +269,47 @@ dv_kernel(const __grid_constant__ CUtensorMap tm_Pd,   // aligned: (skv, sq, bh_
     }
   }
 
+  else if (FPM) {
+    // convert warps 6..13: A tile (P, two 64-column SW128 halves of 64 rows) -> P_drop in place.
+    // 16-byte chunk c (8 columns) of row r sits at chunk c ^ (r % 8); its 8 mask bytes are the
+    // low or high half of mask chunk (4·half + c/2) of the same row (128 B rows, SW128).
+    const int t = int(threadIdx.x) - 6 * 32;   // 0..255
+    const uint64_t s2 = f2(prm.scale, prm.scale);
+    uint32_t si = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      for (int g = 0; g < kGroups; ++g) {
+        for (int kc = 0; kc < n_kc; ++kc, ++si) {
+          const int s = si % ST;
+          if (!warp_wait(&full[s], (si / ST) & 1, abort_flag, err, 0x1501)) goto convert_done;
+          const uint32_t a = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t mk = smem_u32(smem + C::OFF_MSK + s * C::MSK_BYTES);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int f = t + 256 * i;          // 1024 chunks: (half, row, chunk)
+            const int hf = f >> 9, r = (f >> 3) & 63, c = f & 7;
+            const uint32_t pa = a + hf * (A_BYTES / 2) + r * 128 + ((c ^ (r & 7)) << 4);
+            const int q = 4 * hf + (c >> 1);
+            uint32_t mw[2];
+            asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(mw[0]), "=r"(mw[1])
+                         : "r"(mk + r * 128 + ((q ^ (r & 7)) << 4) + (c & 1) * 8));
+            const uint4 pv = lds128(pa);
+            uint32_t w[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // bf16 pair k (elements 2k, 2k+1): mask bytes 2k, 2k+1 of the 8
+              const uint32_t m16 = __byte_perm(mw[k >> 1], 0u, (k & 1) ? 0x4342u : 0x4140u) * 0xFFFFu;
+              w[k] = pack_bf16x2_f2(f2_mul(bf16x2_to_f2(w[k]), s2)) & m16;
+            }
+            sts128(pa, make_uint4(w[0], w[1], w[2], w[3]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_ready[s]);
+        }
+      }
+    }
+  convert_done:;
+  }
   else if (RAG && warp == 14) {
     // raw P_drop producer: runs up to RST K chunks ahead of the re-align warps, independent
     // of the operand ring (which waits for the MMA)

@@ -100,3 +100,11 @@ def test_options_set_get_restore_without_gpu():
         ab.options(no_such_option=1)
     assert lib.attn_bwd_b200_set_option(99, 1) == _lib.EINVAL
     assert lib.attn_bwd_b200_get_option(99) == -2
+
+
+def test_from_mask_rejects_bad_dropout_without_device():
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    for p in (-0.1, 1.0, float("nan")):
+        rc = lib.attn_bwd_b200_shard_from_mask(nul, nul, nul, nul, p, 1, 4, 16, 0, 8, nul, nul, nul)
+        assert rc == _lib.EINVAL
